@@ -1,0 +1,426 @@
+#!/usr/bin/env python3
+"""Benchmark of the NVFP4 paged KV-cache read path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dense8k|dense128k|sparse]
+                    [--impl ours|reference]
+
+Default workload = BASELINE config 2: dense MLA decode over the 288-byte NVFP4 paged pool,
+batch 16 sequences x 8192 tokens, 64 query heads, qk 576 / v 512, page 64, page tables from
+randperm, q and latent ~N(0,1) bf16 (synthetic, seeded).  One step = one fused
+gather + dequant + MLA decode call (decode kernel + split combine) over the batch for one
+layer; steps rotate over enough layer pools that the data read per cycle exceeds the 126 MB
+L2 (8 x 37.7 MB for config 2), so timed steps read the KV bytes from HBM.
+
+value  = KV bytes read (288 B per attended token row) per second, whole job (all ranks),
+         device-timed with CUDA events over exactly K steps replayed from CUDA graphs.
+e2e    = the same metric through the public API (glm53_nvfp4_runtime.mla_decode), eager,
+         with the per-step q / page-table / seq_lens host->device copies and the output
+         device->host copy (pinned buffers) inside the timed region.
+Multi-GPU (torchrun): each rank owns its own 16 sequences and their pages (weak scaling);
+NCCL is used after the timed loop only, to gather the outputs and the max time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "KV-read GB/s (% of 8 TB/s) + decode-attn tokens/s at 1/2/4/8 B200"
+NV_BYTES = 288
+L2_BYTES = 126 * 1024 * 1024
+
+WORKLOADS = {
+    "dense8k": dict(desc="config 2: dense NVFP4 MLA decode, batch 16 x 8192 tokens, 64 heads, "
+                         "qk 576 / v 512, page 64, randperm page table",
+                    B=16, H=64, QL=1, ctx=8192, topk=0),
+    "dense128k": dict(desc="config 2 at 128K context: batch 16 x 131072 tokens, 64 heads",
+                      B=16, H=64, QL=1, ctx=131072, topk=0),
+    "sparse": dict(desc="config 3: sparse top-2048 decode, batch 16, 64 heads, 128K-token "
+                        "sequences on shuffled pages, indices drawn without replacement",
+                   B=16, H=64, QL=1, ctx=131072, topk=2048),
+}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(workload: str):
+    """Per-launch DRAM bytes of the decode kernel from a committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", f"mla_decode_{workload}.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while the GPU is busy."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int):
+        self.samples = []
+        self.ok = False
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:  # noqa: BLE001 - NVML missing: report clocks as unavailable
+            self.max_mhz = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((time.perf_counter(), mhz, rs))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.005)
+
+    def start(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+
+    def stop(self):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self, t0=None, t1=None):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        inside = [s for s in self.samples if t0 is not None and t0 <= s[0] <= t1]
+        use = inside if len(inside) >= 3 else self.samples
+        busy = [s for s in use if not (s[2] & 0x1)] or use
+        reasons = set()
+        for _, _, rs in busy:
+            for bit, name in self.REASONS.items():
+                if rs & bit and bit != 0x1:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(s[1] for s in busy), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(busy),
+                "window": "timed" if use is inside else "soak+timed"}
+
+
+# ---------------------------------------------------------------------------- setup
+def make_layers(rt, torch, wl, layers, dev, seed):
+    """Per layer: a pool written by the append kernel, page tables / top-k rows, q."""
+    B, H, QL, ctx, topk = wl["B"], wl["H"], wl["QL"], wl["ctx"], wl["topk"]
+    pages = B * ctx // 64
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    out = []
+    shared_pool = None
+    for layer in range(layers):
+        if topk == 0 or shared_pool is None:
+            pool = torch.empty(pages, 64, NV_BYTES, dtype=torch.uint8, device=dev)
+            torch.manual_seed(seed * 1000 + layer)
+            for c in range(0, pages * 64, 1 << 20):
+                n = min(1 << 20, pages * 64 - c)
+                x = torch.randn(n, 512, device=dev).to(torch.bfloat16)
+                rt.write_nvfp4(x, pool, torch.arange(c, c + n, device=dev))
+            if topk:
+                shared_pool = pool
+        else:
+            pool = shared_pool                      # sparse layers: one pool, fresh top-k sets
+        page_table = torch.randperm(pages, generator=g).view(B, ctx // 64)
+        if topk:
+            logical = torch.stack([torch.randperm(ctx, generator=g)[:topk] for _ in range(B)])
+            tables = (page_table.gather(1, logical // 64) * 64 + logical % 64).to(torch.int32)
+            tables = tables.view(B, 1, topk)
+            seq = torch.full((B,), topk, dtype=torch.int32)
+        else:
+            tables = page_table.to(torch.int32)
+            seq = torch.full((B,), ctx, dtype=torch.int32)
+        q = torch.randn(B, QL, H, 576, generator=g).to(torch.bfloat16)
+        out.append(dict(pool=pool, tables=tables.to(dev), seq=seq.to(dev), q=q.to(dev),
+                        out=torch.empty(B, QL, H, 512, dtype=torch.bfloat16, device=dev),
+                        tables_h=tables.pin_memory(), seq_h=seq.pin_memory(), q_h=q.pin_memory()))
+    return out
+
+
+def kv_bytes_per_step(wl) -> int:
+    rows = wl["B"] * (wl["topk"] if wl["topk"] else wl["ctx"])
+    return rows * NV_BYTES
+
+
+# ---------------------------------------------------------------------------- CPU side
+def cpu_decode_sample(wl, seconds: float):
+    """The oracle (CPU restatement of the reference path) on a bounded sample: whole
+    sequences of the workload (dequantise + fp32 attention), repeated for ~`seconds`."""
+    import numpy as np
+    import torch
+
+    from oracle import oracle as O
+
+    ctx = wl["topk"] if wl["topk"] else min(wl["ctx"], 8192)
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(ctx, 512, generator=g).to(torch.bfloat16)
+    pool = O.quant_new(x)
+    q = torch.randn(1, wl["QL"], wl["H"], 576, generator=g).float().numpy()
+    if wl["topk"]:
+        tables, seq, sparse = np.arange(ctx, dtype=np.int32).reshape(1, 1, ctx), np.array([ctx]), True
+    else:
+        pool = np.concatenate([pool, np.zeros(((-ctx) % 64, NV_BYTES), np.uint8)])
+        tables, seq, sparse = np.arange(pool.shape[0] // 64, dtype=np.int32)[None], np.array([ctx]), False
+    sm = 1.0 / math.sqrt(576)
+    runs, t0 = 0, time.perf_counter()
+    while True:
+        O.mla_decode(q, pool, tables, seq, sparse=sparse, bmm1_scale=sm, dtype=np.float32)
+        runs += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    gbs = runs * ctx * NV_BYTES / el / 1e9
+    return gbs, el / runs, ctx
+
+
+def reference_arm(args, wl):
+    """--impl reference: the CPU restatement of the reference path (the reference's own code
+    is Python + Triton and is not available on the GPU host), rank 0 only."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import numpy as np  # noqa: F401
+
+    cores = os.cpu_count()
+    cpu_decode_sample(wl, 0.0)                     # warm: build oracle, fault pages in
+    times = []
+    for i in range(args.warmup + args.steps):
+        gbs, per, ctx = cpu_decode_sample(wl, 0.0)
+        if i >= args.warmup:
+            times.append(per)
+    per = sum(times) / len(times)
+    value = ctx * NV_BYTES / per / 1e9
+    sample = (f"one sequence of the workload per step ({ctx} tokens x {wl['H']} heads): oracle "
+              f"dequantise (C) + numpy fp32 attention on {cores} host threads ({cpu_model()})")
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) latent and q)",
+            "config": {"workload": wl["desc"], "global_batch": wl["B"] * args.gpus,
+                       "seq_len": wl["topk"] or wl["ctx"], "parallelism": f"sequence-partitioned x{args.gpus}"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------- GPU side
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--workload", default="dense8k", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        reference_arm(args, wl)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from glm53_flash_dual_dgx_spark_b200 import glm53_nvfp4_runtime as rt
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    kvb = kv_bytes_per_step(wl)
+    # layers so that one rotation reads more than L2 (sparse: distinct top-k sets)
+    touched = kvb
+    layers = max(1, math.ceil(2 * L2_BYTES / touched)) if wl["topk"] == 0 else 32
+    layers = min(layers, 32)
+    L = make_layers(rt, torch, wl, layers, dev, seed=1 + rank)
+    sm = 1.0 / math.sqrt(576)
+
+    def call(ly, out=None):
+        return rt.mla_decode(ly["q"], ly["pool"], None, 128, 512, 64, ly["tables"], ly["seq"],
+                             wl["topk"] or wl["ctx"], sparse_mla_top_k=wl["topk"],
+                             out=ly["out"] if out is None else out, bmm1_scale=sm, bmm2_scale=1.0)
+
+    for ly in L:                                   # eager warm-up (allocates the workspace once)
+        call(ly)
+    torch.cuda.synchronize()
+    graphs = []
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for ly in L:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=s):
+                call(ly)
+            graphs.append(gr)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    launches_per_step = 2 if rt.mla_decode_workspace_size(wl["B"], wl["QL"], wl["H"], wl["ctx"],
+                                                          wl["topk"], dev) > 0 else 1
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    soak_end = time.perf_counter() + 1.0           # clocks settle under load first
+    k = 0
+    while time.perf_counter() < soak_end or k < args.warmup:
+        graphs[k % layers].replay()
+        k += 1
+        if k % 64 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for k in range(args.steps):
+        graphs[k % layers].replay()
+    ev1.record()
+    ev1.synchronize()
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    if world > 1:
+        dist.barrier()
+    sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    t_max = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms_max = float(t_max.item())
+    sec = ms_max / 1e3
+    value = kvb * args.steps * world / sec / 1e9
+    tokens_s = wl["B"] * wl["QL"] * args.steps * world / sec
+
+    # ---- end to end through the public API (eager, host buffers, copies in the region)
+    e2e_steps = max(args.e2e_steps, 10)
+    q_h = [ly["q_h"] for ly in L]
+    out_h = torch.empty(wl["B"], wl["QL"], wl["H"], 512, dtype=torch.bfloat16).pin_memory()
+    h2d = L[0]["q_h"].numel() * 2 + L[0]["tables_h"].numel() * 4 + L[0]["seq_h"].numel() * 4
+    d2h = out_h.numel() * 2
+    qd = torch.empty_like(L[0]["q"])
+    td = torch.empty_like(L[0]["tables"])
+    sd = torch.empty_like(L[0]["seq"])
+    od = torch.empty_like(L[0]["out"])
+    for k in range(3):
+        ly = L[k % layers]
+        qd.copy_(q_h[k % layers], non_blocking=True)
+        call(dict(ly, q=qd), out=od)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for k in range(e2e_steps):
+        ly = L[k % layers]
+        qd.copy_(ly["q_h"], non_blocking=True)
+        td.copy_(ly["tables_h"], non_blocking=True)
+        sd.copy_(ly["seq_h"], non_blocking=True)
+        rt.mla_decode(qd, ly["pool"], None, 128, 512, 64, td, sd, wl["topk"] or wl["ctx"],
+                      sparse_mla_top_k=wl["topk"], out=od, bmm1_scale=sm, bmm2_scale=1.0)
+        out_h.copy_(od, non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = kvb * e2e_steps * world / (float(e_ms.item()) / 1e3) / 1e9
+
+    # ---- outputs of every rank gathered once, after timing (the only collective)
+    if world > 1:
+        gathered = [torch.empty_like(L[0]["out"]) for _ in range(world)]
+        dist.all_gather(gathered, L[0]["out"])
+        torch.cuda.synchronize()
+
+    errors = rt.device_errors(dev)
+    if rank == 0:
+        peak, peak_kind = load_peaks()
+        achieved = kvb / (ms_max / 1e3 / args.steps) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded N(0,1) latent quantised by the append kernel; N(0,1) q)",
+            "config": {"workload": wl["desc"], "global_batch": wl["B"] * world,
+                       "seq_len": wl["ctx"], "topk": wl["topk"], "heads": wl["H"], "q_len": wl["QL"],
+                       "layers_rotated": layers,
+                       "l2": f"inputs larger than L2: {layers} layer(s) x {kvb / 2**20:.1f} MiB read per rotation",
+                       "parallelism": f"sequence-partitioned x{world} (weak scaling)"},
+            "decode_tokens_per_s": round(tokens_s, 1),
+            "kv_rows_per_s": round(kvb * args.steps * world / sec / NV_BYTES, 1),
+            "hbm_frac_of_8tbs": round(value / world / 8000.0, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": profile_traffic(args.workload),
+                         "per_launch_bytes": kvb, "kernel": "mla_decode_kernel (+ split combine)"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+            "gpu_launches": args.steps * launches_per_step,
+            "clocks": sampler.summary(t0, t1),
+            "device_errors": errors,
+        }
+        if world == 1:
+            gbs, per, ctx = cpu_decode_sample(wl, args.cpu_seconds)
+            line["cpu_baseline"] = {
+                "value": round(gbs, 4), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+                "sample": f"oracle decode of one {ctx}-token sequence x {wl['H']} heads repeated for "
+                          f"~{args.cpu_seconds:.0f} s ({per * 1e3:.1f} ms each; C dequantise + numpy "
+                          f"fp32 attention; {cpu_model()})"}
+        print(json.dumps(line), flush=True)
+    del graphs
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

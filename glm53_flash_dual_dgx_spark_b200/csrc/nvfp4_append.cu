@@ -1,0 +1,154 @@
+// Quantize-on-append: bf16/fp16 MLA latent rows -> 288-byte NVFP4 pool rows.
+//
+// Restates _quant_kernel (reference nvfp4-kv/glm53_nvfp4_runtime.py:37-65) for sm_100a:
+// one warp per token, two fully coalesced 16-byte loads per lane (elements [8l, 8l+8) and
+// [256+8l, 256+8l+8)), the block amax completed with one shuffle (a 16-element block spans
+// two neighbouring lanes), and coalesced 4-byte code stores / 1-byte scale stores.
+//
+// Bit-exactness.  The reference computes v = x / s in fp32 and walks the ladder
+// `|v| < 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5` (ties go up; NaN fails every `<`).  Here the
+// division is replaced by the exact comparison |x| < t*s: t*s has at most 7 significant
+// bits and so is exact in fp32, and a bf16/fp16 x can never lie within half an fp32 ulp of
+// t*s without being equal to it, so fl(x/s) < t  <=>  |x| < t*s.  s == 0 makes every
+// threshold 0 and every code 7, like x/0 = +-inf and 0/0 = NaN in the reference; the sign
+// nibble is (x < 0), which equals (x/s < 0) for every s >= 0 and a bf16/fp16 x.
+#include "abi_common.h"
+#include "common.cuh"
+
+namespace nvfp4kv {
+namespace {
+
+template <int DT>
+__device__ __forceinline__ float to_f32(uint16_t v) {
+    if constexpr (DT == NVFP4KV_DTYPE_BF16) return __uint_as_float(static_cast<uint32_t>(v) << 16);
+    else return __half2float(__ushort_as_half(v));
+}
+
+template <int DT, bool VEC>
+__device__ __forceinline__ void load8(const uint16_t* p, float (&x)[8]) {
+    if constexpr (VEC) {
+        uint4 u = *reinterpret_cast<const uint4*>(p);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            x[2 * j] = to_f32<DT>(static_cast<uint16_t>(w[j] & 0xFFFFu));
+            x[2 * j + 1] = to_f32<DT>(static_cast<uint16_t>(w[j] >> 16));
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[j] = to_f32<DT>(p[j]);
+    }
+}
+
+// Code of one element given the block's 7 exact thresholds t_k * s (see file comment).
+__device__ __forceinline__ uint32_t nvfp4_code(float x, const float (&th)[7]) {
+    const float a = fabsf(x);
+    uint32_t c = 0;
+#pragma unroll
+    for (int k = 0; k < 7; ++k) c += !(a < th[k]) ? 1u : 0u;
+    return c | (x < 0.0f ? 8u : 0u);
+}
+
+// Quantise 8 consecutive elements of one block half: returns the 4 packed code bytes and
+// the block's e4m3 scale byte.  `amax_half` is this lane's |x| max; the block max needs
+// the partner lane (lane ^ 1).
+__device__ __forceinline__ uint32_t quant_half(const float (&x)[8], uint8_t& scale_byte) {
+    float m = fabsf(x[0]);
+#pragma unroll
+    for (int j = 1; j < 8; ++j) m = fmaxf(m, fabsf(x[j]));
+    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+    const float sc = fmaxf(__fdiv_rn(m, 6.0f), 1e-8f);     // runtime:47
+    scale_byte = f32_to_e4m3(sc);
+    const float s = e4m3_to_f32(scale_byte);
+    const float tmul[7] = {0.25f, 0.75f, 1.25f, 1.75f, 2.5f, 3.5f, 5.0f};
+    float th[7];
+#pragma unroll
+    for (int k = 0; k < 7; ++k) th[k] = __fmul_rn(tmul[k], s);
+    uint32_t packed = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t lo = nvfp4_code(x[2 * j], th);
+        const uint32_t hi = nvfp4_code(x[2 * j + 1], th);
+        packed |= (lo | (hi << 4)) << (8 * j);
+    }
+    return packed;
+}
+
+template <int DT, int SLOT_DT, bool VEC>
+__global__ void __launch_bounds__(256)
+append_kernel(const uint16_t* __restrict__ src, int64_t T, int64_t stride,
+              uint8_t* __restrict__ pool, int64_t pool_rows, const void* __restrict__ slot,
+              int32_t* __restrict__ err) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= T) return;
+    int64_t sl;
+    if constexpr (SLOT_DT == NVFP4KV_INDEX_I64) sl = static_cast<const int64_t*>(slot)[t];
+    else sl = static_cast<const int32_t*>(slot)[t];
+    if (sl < 0) return;                                        // runtime:42-43
+    if (sl >= pool_rows) {
+        if (lane == 0) set_error(err, NVFP4KV_DEVERR_BAD_SLOT);
+        return;
+    }
+    const uint16_t* row = src + t * stride;
+    float xa[8], xb[8];
+    load8<DT, VEC>(row + 8 * lane, xa);
+    load8<DT, VEC>(row + 256 + 8 * lane, xb);
+    uint8_t sa, sb;
+    const uint32_t ca = quant_half(xa, sa);
+    const uint32_t cb = quant_half(xb, sb);
+    uint8_t* dst = pool + sl * kRowBytes;
+    *reinterpret_cast<uint32_t*>(dst + 4 * lane) = ca;         // bytes [4l, 4l+4)
+    *reinterpret_cast<uint32_t*>(dst + 128 + 4 * lane) = cb;   // bytes [128+4l, ...)
+    if ((lane & 1) == 0) {
+        dst[256 + (lane >> 1)] = sa;                           // block l/2
+        dst[256 + 16 + (lane >> 1)] = sb;                      // block 16 + l/2
+    }
+}
+
+template <int DT, int SLOT_DT>
+void launch_append(const void* kv_c, int64_t T, int64_t stride, uint8_t* pool, int64_t rows,
+                   const void* slot, int32_t* err, cudaStream_t st, bool vec) {
+    const int warps = 8;
+    const dim3 grid(static_cast<unsigned>((T + warps - 1) / warps));
+    const uint16_t* src = static_cast<const uint16_t*>(kv_c);
+    if (vec)
+        append_kernel<DT, SLOT_DT, true><<<grid, warps * 32, 0, st>>>(src, T, stride, pool, rows, slot, err);
+    else
+        append_kernel<DT, SLOT_DT, false><<<grid, warps * 32, 0, st>>>(src, T, stride, pool, rows, slot, err);
+}
+
+}  // namespace
+}  // namespace nvfp4kv
+
+extern "C" int nvfp4kv_append(const void* kv_c, int kv_dtype, int64_t num_tokens, int64_t src_stride,
+                              uint8_t* pool, int64_t pool_rows, const void* slot_mapping,
+                              int slot_dtype, int32_t* err_flag, nvfp4kv_stream_t stream) {
+    using namespace nvfp4kv;
+    if (num_tokens < 0) return fail(NVFP4KV_EINVAL, "nvfp4kv_append: num_tokens < 0");
+    if (num_tokens == 0) return NVFP4KV_OK;                     // runtime:73-74
+    if (!kv_c || !pool || !slot_mapping) return fail(NVFP4KV_EINVAL, "nvfp4kv_append: null pointer");
+    if (src_stride < NVFP4KV_LATENT)
+        return fail(NVFP4KV_EINVAL, "nvfp4kv_append: src_stride %lld < 512", (long long)src_stride);
+    if (pool_rows <= 0) return fail(NVFP4KV_EINVAL, "nvfp4kv_append: empty pool");
+    if (reinterpret_cast<uintptr_t>(pool) % 16 != 0)
+        return fail(NVFP4KV_EINVAL, "nvfp4kv_append: pool must be 16-byte aligned");
+    if (kv_dtype != NVFP4KV_DTYPE_BF16 && kv_dtype != NVFP4KV_DTYPE_F16)
+        return fail(NVFP4KV_EINVAL, "nvfp4kv_append: kv_dtype must be bf16 or fp16");
+    if (slot_dtype != NVFP4KV_INDEX_I64 && slot_dtype != NVFP4KV_INDEX_I32)
+        return fail(NVFP4KV_EINVAL, "nvfp4kv_append: slot dtype must be int64 or int32");
+    const bool vec = (reinterpret_cast<uintptr_t>(kv_c) % 16 == 0) && (src_stride % 8 == 0);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (kv_dtype == NVFP4KV_DTYPE_BF16) {
+        if (slot_dtype == NVFP4KV_INDEX_I64)
+            launch_append<NVFP4KV_DTYPE_BF16, NVFP4KV_INDEX_I64>(kv_c, num_tokens, src_stride, pool, pool_rows, slot_mapping, err_flag, st, vec);
+        else
+            launch_append<NVFP4KV_DTYPE_BF16, NVFP4KV_INDEX_I32>(kv_c, num_tokens, src_stride, pool, pool_rows, slot_mapping, err_flag, st, vec);
+    } else {
+        if (slot_dtype == NVFP4KV_INDEX_I64)
+            launch_append<NVFP4KV_DTYPE_F16, NVFP4KV_INDEX_I64>(kv_c, num_tokens, src_stride, pool, pool_rows, slot_mapping, err_flag, st, vec);
+        else
+            launch_append<NVFP4KV_DTYPE_F16, NVFP4KV_INDEX_I32>(kv_c, num_tokens, src_stride, pool, pool_rows, slot_mapping, err_flag, st, vec);
+    }
+    return check_launch("nvfp4kv_append");
+}

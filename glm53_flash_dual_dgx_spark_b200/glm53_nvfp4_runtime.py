@@ -1,0 +1,307 @@
+"""Drop-in NVFP4 KV-pool runtime for B200 (sm_100a).
+
+Same module surface as the reference's ``nvfp4-kv/glm53_nvfp4_runtime.py``
+(Plaaasma/glm53-flash-dual-dgx-spark), which the vLLM seam patcher copies into the vLLM
+package as ``vllm.glm53_nvfp4_runtime``:
+
+    NV_BYTES, DS_BYTES, enabled(), write_nvfp4(), _gather(), build_scratch(),
+    _SYNC_FREE_T, _bufs
+
+plus the fused read path the reference does not have:
+
+    mla_decode(query, kv_cache, workspace_buffer, qk_nope_head_dim, kv_lora_rank,
+               qk_rope_head_dim, block_tables, seq_lens, max_seq_len,
+               sparse_mla_top_k=0, out=None, bmm1_scale=1.0, bmm2_scale=1.0)
+
+argument-compatible with FlashInfer's ``trtllm_batch_decode_with_kv_cache_mla`` (the
+consumer the reference feeds, patch_nvfp4_kv.py:84-118) but reading the 288-byte pool
+rows directly instead of a 656-byte fp8 scratch.
+
+Every compute call goes through the C ABI of ``libnvfp4kv.so`` on the current torch CUDA
+stream; nothing synchronises the host and nothing falls back to the CPU.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+from . import _lib
+
+NV_BYTES = 288
+DS_BYTES = 656
+LATENT = 512
+
+_ON = os.environ.get("GLM53_NVFP4_KV", "0") == "1"          # read once at import (runtime:29)
+
+# Sync-free ceiling of build_scratch (runtime:134-140): steps with at most this many query
+# tokens gather every table entry into a persistent buffer (no host sync, graph-safe).
+_SYNC_FREE_T = int(os.environ.get("GLM53_NVFP4_SYNCFREE_T", "192"))
+
+# Persistent device buffers keyed like the reference's: ("shared", K, device index) for the
+# build_scratch buffer; ("err", index) / ("ws", index) for this module's own state.
+_bufs: dict = {}
+
+
+def enabled() -> bool:
+    return _ON
+
+
+# ------------------------------------------------------------------ helpers
+def _stream(dev: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (this runtime has no CPU path)")
+
+
+def _err_word(dev: torch.device) -> torch.Tensor:
+    key = ("err", dev.index)
+    e = _bufs.get(key)
+    if e is None:
+        e = torch.zeros(1, dtype=torch.int32, device=dev)
+        _bufs[key] = e
+    return e
+
+
+def device_errors(device=None, clear: bool = True) -> int:
+    """Read (and by default clear) the device error word: OR of NVFP4KV_DEVERR_* bits.
+
+    Synchronises with the device; meant for tests and health checks, not the hot path.
+    """
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    e = _err_word(dev)
+    v = int(e.item())
+    if clear:
+        e.zero_()
+    return v
+
+
+class _on_device:
+    """Make `dev` current for the C call when it is not already (launches use it)."""
+
+    def __init__(self, dev: torch.device):
+        self.dev = dev
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.dev.index:
+            self.prev = cur
+            torch.cuda.set_device(self.dev)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
+# ------------------------------------------------------------------ write path
+def write_nvfp4(kv_c: torch.Tensor, kv_cache: torch.Tensor, slot_mapping: torch.Tensor) -> None:
+    """kv_c [T, 512] -> NVFP4 rows at slot_mapping in kv_cache (viewed [-1, 288]).
+
+    Same contract as the reference (runtime:68-76): T == 0 is a no-op, slots < 0 are
+    skipped.  Slots past the pool are skipped too and flagged in the device error word.
+    """
+    pool = kv_cache.view(-1, NV_BYTES)
+    T = kv_c.shape[0]
+    if T == 0:
+        return
+    _require_cuda(kv_c, "kv_c")
+    _require_cuda(pool, "kv_cache")
+    if kv_c.dtype == torch.bfloat16:
+        dt = _lib.DTYPE_BF16
+    elif kv_c.dtype == torch.float16:
+        dt = _lib.DTYPE_F16
+    else:
+        raise TypeError(f"kv_c must be bfloat16 or float16, got {kv_c.dtype}")
+    if kv_c.dim() != 2 or kv_c.shape[1] < LATENT or kv_c.stride(1) != 1:
+        raise ValueError("kv_c must be [T, >=512] with a contiguous last dimension")
+    if pool.dtype != torch.uint8:
+        raise TypeError("kv_cache must be a uint8 pool")
+    slot = slot_mapping.reshape(-1)
+    if slot.numel() != T:
+        raise ValueError(f"slot_mapping has {slot.numel()} entries for {T} tokens")
+    if slot.dtype == torch.int64:
+        sdt = _lib.INDEX_I64
+    elif slot.dtype == torch.int32:
+        sdt = _lib.INDEX_I32
+    else:
+        raise TypeError("slot_mapping must be int64 or int32")
+    slot = slot.contiguous()
+    dev = kv_c.device
+    with _on_device(dev):
+        rc = _lib.lib().nvfp4kv_append(kv_c.data_ptr(), dt, T, kv_c.stride(0), pool.data_ptr(),
+                                       pool.shape[0], slot.data_ptr(), sdt,
+                                       _err_word(dev).data_ptr(), _stream(dev))
+    _lib.check(rc, "nvfp4kv_append")
+
+
+# ------------------------------------------------------------------ 656-byte read path
+def _gather(pool: torch.Tensor, idx: torch.Tensor, out: torch.Tensor) -> None:
+    """NVFP4 pool rows at idx -> fp8_ds_mla 656-byte rows in out (runtime:128-131)."""
+    S = idx.shape[0]
+    if S == 0:
+        return
+    _require_cuda(pool, "pool")
+    if idx.dtype != torch.int32:
+        raise TypeError("idx must be int32")
+    if out.dtype != torch.uint8 or out.shape[-1] != DS_BYTES or not out.is_contiguous():
+        raise ValueError("out must be a contiguous [S, 656] uint8 tensor")
+    idx = idx.contiguous()
+    dev = pool.device
+    with _on_device(dev):
+        rc = _lib.lib().nvfp4kv_gather_ds656(pool.data_ptr(), pool.shape[0], idx.data_ptr(), S,
+                                             out.data_ptr(), _stream(dev))
+    _lib.check(rc, "nvfp4kv_gather_ds656")
+
+
+def build_scratch(kv_cache: torch.Tensor, block_tables: torch.Tensor):
+    """kv_cache: allocated pool (any shape, 288 B/token rows).
+    block_tables: [T, 1, K] int32 physical token rows (-1 padded).
+    Returns (scratch [P, 64, 656] uint8, tables [T, 1, K] into scratch), as the reference
+    (runtime:143-182): T <= _SYNC_FREE_T gathers every entry into a persistent buffer with
+    fixed shapes and no host sync; larger T deduplicates with torch.unique first.
+    """
+    pool = kv_cache.view(-1, NV_BYTES)
+    T, one, K = block_tables.shape
+    flat = block_tables.view(-1)
+    dev = pool.device
+    if T <= _SYNC_FREE_T:
+        S = T * K
+        P = (S + 63) // 64
+        key = ("shared", K, dev.index)
+        ent = _bufs.get(key)
+        if ent is None:
+            pcap = (_SYNC_FREE_T * K + 63) // 64
+            ent = (torch.zeros(pcap, 64, DS_BYTES, dtype=torch.uint8, device=dev),
+                   torch.arange(pcap * 64, dtype=torch.int32, device=dev))
+            _bufs[key] = ent
+        buf, ar = ent
+        _gather(pool, flat, buf.view(-1, DS_BYTES)[:S])
+        return buf[:P], ar[:S].view(T, 1, K)
+    uniq, inv = torch.unique(flat, return_inverse=True)
+    S = uniq.shape[0]
+    P = (S + 63) // 64
+    scratch = torch.zeros(P, 64, DS_BYTES, dtype=torch.uint8, device=dev)
+    _gather(pool, uniq.to(torch.int32), scratch.view(-1, DS_BYTES)[:S])
+    return scratch, inv.to(torch.int32).view(T, 1, K)
+
+
+def dequant(kv_cache: torch.Tensor, rows: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Pool rows -> bf16 [n, 512] (exact); rows outside the pool (and -1) read as zeros."""
+    pool = kv_cache.view(-1, NV_BYTES)
+    rows = rows.reshape(-1)
+    n = rows.numel()
+    if out is None:
+        out = torch.empty(n, LATENT, dtype=torch.bfloat16, device=pool.device)
+    if n == 0:
+        return out
+    _require_cuda(pool, "kv_cache")
+    if rows.dtype == torch.int64:
+        rdt = _lib.INDEX_I64
+    elif rows.dtype == torch.int32:
+        rdt = _lib.INDEX_I32
+    else:
+        raise TypeError("rows must be int64 or int32")
+    if out.dtype != torch.bfloat16 or not out.is_contiguous() or out.numel() < n * LATENT:
+        raise ValueError("out must be a contiguous bf16 [n, 512] tensor")
+    rows = rows.contiguous()
+    dev = pool.device
+    with _on_device(dev):
+        rc = _lib.lib().nvfp4kv_dequant_bf16(pool.data_ptr(), pool.shape[0], rows.data_ptr(), rdt, n,
+                                             out.data_ptr(), _err_word(dev).data_ptr(), _stream(dev))
+    _lib.check(rc, "nvfp4kv_dequant_bf16")
+    return out
+
+
+# ------------------------------------------------------------------ fused read path
+def mla_decode_workspace_size(batch: int, q_len: int, num_heads: int, max_seq_len: int,
+                              sparse_mla_top_k: int = 0, device=None) -> int:
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    out = ctypes.c_size_t(0)
+    with _on_device(dev):
+        rc = _lib.lib().nvfp4kv_mla_decode_workspace_size(batch, q_len, num_heads, max_seq_len,
+                                                          sparse_mla_top_k, ctypes.byref(out))
+    _lib.check(rc, "nvfp4kv_mla_decode_workspace_size")
+    return int(out.value)
+
+
+def _workspace(dev: torch.device, nbytes: int, given: torch.Tensor | None) -> torch.Tensor | None:
+    if nbytes == 0:
+        return None
+    if given is not None and given.is_cuda and given.numel() * given.element_size() >= nbytes \
+            and given.data_ptr() % 256 == 0 and given.is_contiguous():
+        return given
+    key = ("ws", dev.index)
+    ws = _bufs.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+        _bufs[key] = ws
+    return ws
+
+
+def mla_decode(query: torch.Tensor, kv_cache: torch.Tensor, workspace_buffer: torch.Tensor | None,
+               qk_nope_head_dim: int, kv_lora_rank: int, qk_rope_head_dim: int,
+               block_tables: torch.Tensor, seq_lens: torch.Tensor, max_seq_len: int,
+               sparse_mla_top_k: int = 0, out: torch.Tensor | None = None,
+               bmm1_scale: float = 1.0, bmm2_scale: float = 1.0) -> torch.Tensor:
+    """Fused NVFP4 gather + MLA decode (see module docstring).
+
+    query: [B, q_len, H, kv_lora_rank + qk_rope_head_dim] bf16.
+    kv_cache: the 288-byte pool, [num_pages, page_size, 288] (or [num_pages, 1, page_size,
+      288]); page_size is read from dim -2.
+    Dense (sparse_mla_top_k == 0): block_tables [B, max_pages] page ids, seq_lens = context
+      lengths.  Sparse: block_tables [B, 1, K] or [B, K] physical token rows (-1 padded),
+      seq_lens = number of leading entries to use.
+    Returns out [B, q_len, H, kv_lora_rank] bf16.  ``workspace_buffer`` is used for the
+    split partials when it is large enough, else a persistent per-device buffer is.
+    """
+    del qk_nope_head_dim  # accepted for signature compatibility; MLA absorbed form ignores it
+    _require_cuda(query, "query")
+    _require_cuda(kv_cache, "kv_cache")
+    if isinstance(bmm1_scale, torch.Tensor) or isinstance(bmm2_scale, torch.Tensor):
+        raise TypeError("bmm1_scale / bmm2_scale must be Python floats (a device scalar would need a sync)")
+    if query.dtype != torch.bfloat16 or query.dim() != 4:
+        raise ValueError("query must be a 4-D bf16 tensor [B, q_len, H, D]")
+    if query.stride(3) != 1:
+        raise ValueError("query's last dimension must be contiguous")
+    B, QL, H, D = query.shape
+    if kv_lora_rank != LATENT or D != kv_lora_rank + qk_rope_head_dim:
+        raise ValueError(f"query dim {D} must equal kv_lora_rank (512) + qk_rope_head_dim")
+    pool = kv_cache.view(-1, NV_BYTES)
+    page_size = kv_cache.shape[-2] if kv_cache.dim() >= 3 else 64
+    sparse = int(sparse_mla_top_k) > 0
+    if block_tables.dtype != torch.int32 or seq_lens.dtype != torch.int32:
+        raise TypeError("block_tables and seq_lens must be int32")
+    bt = block_tables.reshape(B, -1) if sparse else block_tables
+    if bt.dim() != 2 or bt.stride(1) != 1:
+        raise ValueError("block_tables must be [B, width] with a contiguous last dimension")
+    if sparse and bt.shape[1] < sparse_mla_top_k:
+        raise ValueError("sparse block_tables narrower than sparse_mla_top_k")
+    if not sparse and bt.shape[1] * page_size < max_seq_len:
+        raise ValueError("block_tables too narrow for max_seq_len")
+    sl = seq_lens.contiguous()
+    if out is None:
+        out = torch.empty(B, QL, H, LATENT, dtype=torch.bfloat16, device=query.device)
+    elif out.shape != (B, QL, H, LATENT) or out.dtype != torch.bfloat16 or out.stride(3) != 1:
+        raise ValueError("out must be bf16 [B, q_len, H, 512] with a contiguous last dimension")
+    dev = query.device
+    with _on_device(dev):
+        ws_need = mla_decode_workspace_size(B, QL, H, max_seq_len, int(sparse_mla_top_k), dev)
+        ws = _workspace(dev, ws_need, workspace_buffer)
+        rc = _lib.lib().nvfp4kv_mla_decode(
+            query.data_ptr(), query.stride(0), query.stride(1), query.stride(2),
+            pool.data_ptr(), pool.shape[0],
+            bt.data_ptr(), bt.stride(0), sl.data_ptr(),
+            B, QL, H, D, kv_lora_rank,
+            int(sparse_mla_top_k), int(page_size), int(max_seq_len),
+            float(bmm1_scale), float(bmm2_scale),
+            out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
+            ws.data_ptr() if ws is not None else None, ws_need,
+            _err_word(dev).data_ptr(), _stream(dev))
+    _lib.check(rc, "nvfp4kv_mla_decode")
+    return out

@@ -1,0 +1,140 @@
+/*
+ * nvfp4kv -- C ABI of the B200 (sm_100a) NVFP4 paged KV-cache library.
+ *
+ * Pool layout (one row per token, 288 bytes, rows 16-byte aligned):
+ *   bytes [0, 256)   : 512 e2m1 codes, byte i = code[2i] | code[2i+1] << 4
+ *   bytes [256, 288) : 32 e4m3 block scales, scale g covers elements [16g, 16g + 16)
+ * A paged pool is [num_pages, page_size, 288]; token slot = page * page_size + offset.
+ * Reference layout: nvfp4-kv/glm53_nvfp4_runtime.py:4-6, :26, :37-65 and
+ * nvfp4-kv/patch_nvfp4_kv.py:29-53 (Plaaasma/glm53-flash-dual-dgx-spark).
+ *
+ * Conventions:
+ *   - every pointer is a device pointer unless stated otherwise; the caller owns all memory;
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream);
+ *   - functions return NVFP4KV_OK or an NVFP4KV_E* code and never synchronize;
+ *     nvfp4kv_last_error() gives a message for the calling thread's last failure;
+ *   - `err_flag` (may be NULL) is a device int32 the kernels OR NVFP4KV_DEVERR_* bits into
+ *     when they meet out-of-range slots / indices / pages or a wait that timed out.  Bad
+ *     entries are masked, never dereferenced.
+ */
+#ifndef NVFP4KV_H_
+#define NVFP4KV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NVFP4KV_ROW_BYTES 288
+#define NVFP4KV_DS_BYTES 656
+#define NVFP4KV_LATENT 512
+#define NVFP4KV_ROPE 64
+
+/* host-side return codes */
+#define NVFP4KV_OK 0
+#define NVFP4KV_EINVAL 1     /* bad argument (shape, alignment, dtype) */
+#define NVFP4KV_EWORKSPACE 2 /* workspace too small */
+#define NVFP4KV_ECUDA 3      /* a CUDA runtime call failed */
+
+/* device-side error bits (OR-ed into *err_flag) */
+#define NVFP4KV_DEVERR_TIMEOUT 1    /* a bounded wait gave up */
+#define NVFP4KV_DEVERR_BAD_SLOT 2   /* append slot >= pool_rows (row skipped) */
+#define NVFP4KV_DEVERR_BAD_INDEX 4  /* sparse index < -1 or >= pool_rows (masked) */
+#define NVFP4KV_DEVERR_BAD_PAGE 8   /* page id < 0 or >= num_pages (masked) */
+#define NVFP4KV_DEVERR_SEQ_LEN 16   /* seq_len beyond the table / top-k width (clamped) */
+
+/* input element types */
+#define NVFP4KV_DTYPE_BF16 0
+#define NVFP4KV_DTYPE_F16 1
+/* index element types */
+#define NVFP4KV_INDEX_I64 0
+#define NVFP4KV_INDEX_I32 1
+
+typedef struct CUstream_st* nvfp4kv_stream_t;
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int nvfp4kv_version(void);
+
+/* Message describing the calling thread's last non-OK return ("" if none). */
+const char* nvfp4kv_last_error(void);
+
+/*
+ * Quantize-on-append.  Replaces _quant_kernel + write_nvfp4
+ * (nvfp4-kv/glm53_nvfp4_runtime.py:37-76), which the write seam calls from
+ * do_kv_cache_update (nvfp4-kv/patch_nvfp4_kv.py:67-72).
+ *
+ * kv_c: [num_tokens, >=512] bf16/fp16 with row stride `src_stride` elements (inner dim
+ * contiguous); token t is quantised into pool row slot[t].  slot < 0 skips the token (as
+ * the reference does); slot >= pool_rows skips it and sets NVFP4KV_DEVERR_BAD_SLOT.
+ * Bit-exact with the reference: per-16 scale = e4m3_rne(max(amax/6, 1e-8)), code by the
+ * reference's `<` threshold ladder on x / scale (ties go up), sign = (x / scale < 0).
+ * num_tokens == 0 is a no-op.
+ */
+int nvfp4kv_append(const void* kv_c, int kv_dtype, int64_t num_tokens, int64_t src_stride,
+                   uint8_t* pool, int64_t pool_rows, const void* slot_mapping, int slot_dtype,
+                   int32_t* err_flag, nvfp4kv_stream_t stream);
+
+/*
+ * 656-byte fp8_ds_mla gather.  Replaces _gather_kernel + _gather
+ * (nvfp4-kv/glm53_nvfp4_runtime.py:87-131); build_scratch (:143-182) calls it.
+ * out: [num_rows, 656] bytes; row r is pool row clamp(idx[r], 0, pool_rows-1) re-encoded
+ * as 512 e4m3 bytes (per-128 scale = max(amax/448, 1e-12), stored as fp32 at 512+4j)
+ * followed by 128 zero bytes.  Byte-identical to the reference.
+ */
+int nvfp4kv_gather_ds656(const uint8_t* pool, int64_t pool_rows, const int32_t* idx,
+                         int64_t num_rows, uint8_t* out, nvfp4kv_stream_t stream);
+
+/*
+ * Dequantise pool rows to bf16: out[r, :] = decode(pool[rows[r]]) for 0 <= rows[r] <
+ * pool_rows, zeros otherwise (NVFP4KV_DEVERR_BAD_INDEX for rows < -1 or >= pool_rows).
+ * The values (code x block scale) are exact in bf16.  The reference has no standalone
+ * equivalent; it is the decode half of _gather_kernel (:99-108) without the fp8 re-encode.
+ */
+int nvfp4kv_dequant_bf16(const uint8_t* pool, int64_t pool_rows, const void* rows,
+                         int rows_dtype, int64_t num_rows, void* out,
+                         int32_t* err_flag, nvfp4kv_stream_t stream);
+
+/*
+ * Fused NVFP4 gather + dequant + MLA decode attention (tcgen05, split-K + LSE combine).
+ * Replaces build_scratch + trtllm_batch_decode_with_kv_cache_mla at the read seam
+ * (nvfp4-kv/patch_nvfp4_kv.py:84-118; call signature of the consumer:
+ * flashinfer mla/_core.py:598-620, as called in nvfp4-kv/test_kernel_equiv.py:34-39).
+ * It reads the 288-byte pool directly; no scratch rows are materialised.
+ *
+ * q: bf16 [batch, q_len, num_heads, head_dim_qk] with element strides
+ *    (q_stride_b, q_stride_q, q_stride_h) and a contiguous last dim.  Only the first
+ *    kv_lora_rank (512) dims take part: the 288-byte rows carry no rope part (the reference
+ *    drops k_pe, patch_nvfp4_kv.py:70), so the trailing rope dims of q multiply zeros.
+ * Dense mode (sparse_topk == 0): tables [batch, >= ceil(max_seq_len/page_size)] page ids
+ *    (row stride tables_stride), seq_lens[b] = context length.  With q_len > 1 query
+ *    token i sees tokens t < seq_len - (q_len - 1 - i) (causal MTP).
+ * Sparse mode (sparse_topk > 0, q_len must be 1): tables [batch, >= sparse_topk] physical
+ *    pool rows, -1 padded; seq_lens[b] = number of leading entries to use.
+ * out: bf16 [batch, q_len, num_heads, 512] with strides (out_stride_b, out_stride_q,
+ *    out_stride_h): softmax(bmm1_scale * q.k) . v * bmm2_scale, k = v = dequantised rows.
+ *    A query row with no visible token is written as zeros.
+ * workspace: device scratch of at least nvfp4kv_mla_decode_workspace_size() bytes, 256-B
+ *    aligned.  No allocation and no host synchronisation happen inside the call.
+ */
+int nvfp4kv_mla_decode(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,
+                       const uint8_t* pool, int64_t pool_rows,
+                       const int32_t* tables, int64_t tables_stride,
+                       const int32_t* seq_lens,
+                       int batch, int q_len, int num_heads, int head_dim_qk, int kv_lora_rank,
+                       int sparse_topk, int page_size, int max_seq_len,
+                       float bmm1_scale, float bmm2_scale,
+                       void* out, int64_t out_stride_b, int64_t out_stride_q, int64_t out_stride_h,
+                       void* workspace, size_t workspace_bytes,
+                       int32_t* err_flag, nvfp4kv_stream_t stream);
+
+/* Workspace bytes nvfp4kv_mla_decode needs for this shape on the current device. */
+int nvfp4kv_mla_decode_workspace_size(int batch, int q_len, int num_heads, int max_seq_len,
+                                      int sparse_topk, size_t* bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVFP4KV_H_ */

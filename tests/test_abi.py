@@ -1,0 +1,92 @@
+"""CPU: the C-ABI library loads, exports every symbol include/nvfp4kv.h declares, and its
+argument checks reject bad calls before any kernel launch (no GPU needed for these)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+from glm53_flash_dual_dgx_spark_b200 import _lib
+
+HEADER = os.path.join(ROOT, "include", "nvfp4kv.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(nvfp4kv_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    names = declared_functions()
+    assert len(names) == 7, names
+    for n in names:
+        assert hasattr(lib, n), n
+    assert set(names) == set(_lib.SIGNATURES)
+
+
+def test_version_and_empty_error():
+    lib = _lib.lib()
+    assert lib.nvfp4kv_version() >= 100
+    assert isinstance(lib.nvfp4kv_last_error(), bytes)
+
+
+def test_append_argument_checks_without_launch():
+    lib = _lib.lib()
+    assert lib.nvfp4kv_append(None, 0, 0, 512, None, 0, None, 0, None, None) == _lib.OK  # T == 0
+    assert lib.nvfp4kv_append(None, 0, -1, 512, None, 0, None, 0, None, None) == _lib.EINVAL
+    assert lib.nvfp4kv_append(None, 0, 4, 512, None, 16, None, 0, None, None) == _lib.EINVAL
+    assert b"null" in lib.nvfp4kv_last_error()
+    # 8-byte aligned fake pointers never reach a launch: the stride check fails first
+    assert lib.nvfp4kv_append(16, 0, 4, 100, 4096, 16, 64, 0, None, None) == _lib.EINVAL
+    assert b"src_stride" in lib.nvfp4kv_last_error()
+    assert lib.nvfp4kv_append(16, 7, 4, 512, 4096, 16, 64, 0, None, None) == _lib.EINVAL
+    assert lib.nvfp4kv_append(16, 0, 4, 512, 4097, 16, 64, 0, None, None) == _lib.EINVAL  # unaligned pool
+
+
+def test_gather_and_decode_argument_checks_without_launch():
+    lib = _lib.lib()
+    assert lib.nvfp4kv_gather_ds656(None, 1, None, 0, None, None) == _lib.OK
+    assert lib.nvfp4kv_gather_ds656(None, 1, None, 5, None, None) == _lib.EINVAL
+    assert lib.nvfp4kv_gather_ds656(4096, 1, 64, 5, 4100, None) == _lib.EINVAL      # unaligned out
+    args = dict(q=4096, sb=64 * 576, sq=64 * 576, sh=576, pool=4096, rows=1024, tables=64, ts=16,
+                sl=64, B=2, QL=1, H=64, D=576, R=512, topk=0, page=64, msl=1024, s1=1.0, s2=1.0,
+                out=4096, ob=64 * 512, oq=64 * 512, oh=512, ws=None, wsb=0, err=None, st=None)
+
+    def call(**kw):
+        a = dict(args, **kw)
+        return lib.nvfp4kv_mla_decode(a["q"], a["sb"], a["sq"], a["sh"], a["pool"], a["rows"],
+                                      a["tables"], a["ts"], a["sl"], a["B"], a["QL"], a["H"], a["D"],
+                                      a["R"], a["topk"], a["page"], a["msl"], a["s1"], a["s2"],
+                                      a["out"], a["ob"], a["oq"], a["oh"], a["ws"], a["wsb"],
+                                      a["err"], a["st"])
+
+    assert call(B=0) == _lib.OK
+    assert call(R=256) == _lib.EINVAL
+    assert call(D=500) == _lib.EINVAL
+    assert call(topk=2048, QL=3) == _lib.EINVAL
+    assert call(page=48) == _lib.EINVAL
+    assert call(rows=1000) == _lib.EINVAL          # not a multiple of the page size
+    assert call(sh=577) == _lib.EINVAL             # q stride not a multiple of 8
+    assert call(ws=None, wsb=0) == _lib.EWORKSPACE  # 2 sequences x 1024 tokens need splits
+    assert b"workspace" in lib.nvfp4kv_last_error()
+
+
+def test_workspace_size_formula():
+    lib = _lib.lib()
+    out = ctypes.c_size_t()
+    assert lib.nvfp4kv_mla_decode_workspace_size(16, 1, 64, 8192, 0, ctypes.byref(out)) == _lib.OK
+    # 16 query groups on (at least) 148 SMs: 8 splits of 8 tiles; 64 rows x (512 + 2) floats
+    assert out.value == 8 * 16 * 64 * 514 * 4
+    assert lib.nvfp4kv_mla_decode_workspace_size(256, 1, 64, 8192, 0, ctypes.byref(out)) == _lib.OK
+    assert out.value == 0                          # enough query groups: no split, no workspace
+    assert lib.nvfp4kv_mla_decode_workspace_size(-1, 1, 64, 8192, 0, ctypes.byref(out)) == _lib.EINVAL
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", str(tmp_path / "absent.so"))
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        _lib.lib()
