@@ -112,8 +112,9 @@ int nvfp4kv_dequant_bf16(const uint8_t* pool, int64_t pool_rows, const void* row
  *    token i sees tokens t < seq_len - (q_len - 1 - i) (causal MTP).
  * Sparse mode (sparse_topk > 0, q_len must be 1): tables [batch, >= sparse_topk] physical
  *    pool rows, -1 padded; seq_lens[b] = number of leading entries to use.
- * out: bf16 [batch, q_len, num_heads, 512] with strides (out_stride_b, out_stride_q,
- *    out_stride_h): softmax(bmm1_scale * q.k) . v * bmm2_scale, k = v = dequantised rows.
+ * out: bf16 [batch, q_len, num_heads, 512], 16-byte aligned, with strides (out_stride_b,
+ *    out_stride_q, out_stride_h), multiples of 8 elements:
+ *    softmax(bmm1_scale * q.k) . v * bmm2_scale, k = v = dequantised rows.
  *    A query row with no visible token is written as zeros.
  * workspace: device scratch of at least nvfp4kv_mla_decode_workspace_size() bytes, 256-B
  *    aligned.  No allocation and no host synchronisation happen inside the call.

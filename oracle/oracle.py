@@ -177,25 +177,28 @@ def build_scratch(pool: np.ndarray, block_tables, sync_free_t: int = 192):
 
 
 def token_rows(block_tables, seq_lens, page_size: int, sparse: bool, pool_rows: int):
-    """Per batch entry, the list of pool rows it attends to (invalid entries dropped).
+    """Per batch entry, (pool rows, token positions) it attends to, invalid entries dropped.
 
-    Dense: token t < seq_lens[b] lives at row ``block_tables[b, t // page] * page + t % page``.
+    Dense: token t < seq_lens[b] lives at row ``block_tables[b, t // page] * page + t % page``;
+    tokens whose page id is outside the pool are masked.
     Sparse: entries j < seq_lens[b] of ``block_tables[b, 0 or :, j]`` are physical rows;
-    negative or out-of-range rows are masked.
+    negative or out-of-range rows are masked.  The position of entry j is j.
     """
+    num_pages = pool_rows // page_size
     bt = np.asarray(block_tables)
     sl = np.asarray(seq_lens).reshape(-1)
     out = []
     for b in range(sl.shape[0]):
         n = int(sl[b])
+        t = np.arange(n, dtype=np.int64)
         if sparse:
             idx = bt[b].reshape(-1)[:n].astype(np.int64)
-            idx = idx[(idx >= 0) & (idx < pool_rows)]
-            out.append(idx)
+            ok = (idx >= 0) & (idx < pool_rows)
+            out.append((idx[ok], t[ok]))
         else:
-            t = np.arange(n, dtype=np.int64)
             pages = bt[b].reshape(-1)[t // page_size].astype(np.int64)
-            out.append(pages * page_size + t % page_size)
+            ok = (pages >= 0) & (pages < num_pages)
+            out.append(((pages * page_size + t % page_size)[ok], t[ok]))
     return out
 
 
@@ -222,14 +225,15 @@ def mla_decode(q, pool: np.ndarray, block_tables, seq_lens, *, sparse: bool,
     rows = token_rows(block_tables, seq_lens, page_size, sparse, flat_pool.shape[0])
     out = np.zeros((B, QL, H, kv_lora_rank), dtype=dtype)
     lse = np.full((B, QL, H), -np.inf, dtype=dtype)
+    sl = np.asarray(seq_lens).reshape(-1)
     for b in range(B):
-        kv = dequant(flat_pool, rows[b]).astype(dtype)           # [n, 512]
-        n = kv.shape[0]
+        r, pos = rows[b]
+        kv = dequant(flat_pool, r).astype(dtype)                 # [n, 512]
         for i in range(QL):
-            vis = n if sparse else max(0, n - (QL - 1 - i))
-            if vis == 0:
+            lim = int(sl[b]) if sparse else int(sl[b]) - (QL - 1 - i)
+            k = kv[pos < lim]
+            if k.shape[0] == 0:
                 continue
-            k = kv[:vis]
             s = (q[b, i, :, :kv_lora_rank].astype(dtype) @ k.T) * dtype(bmm1_scale)  # [H, vis]
             m = s.max(axis=1, keepdims=True)
             p = np.exp(s - m)
