@@ -134,6 +134,31 @@ int nvfp4kv_mla_decode(const void* q, int64_t q_stride_b, int64_t q_stride_q, in
 int nvfp4kv_mla_decode_workspace_size(int batch, int q_len, int num_heads, int max_seq_len,
                                       int sparse_topk, size_t* bytes);
 
+/* Capacity of the device scratch array behind nvfp4kv_mla_decode_static. */
+#define NVFP4KV_STATIC_SCRATCH_BYTES 33554432u
+
+/*
+ * nvfp4kv_mla_decode without a workspace argument: the split-K partials go to a file-scope
+ * device array of NVFP4KV_STATIC_SCRATCH_BYTES (32 MiB, reserved per device when the module
+ * loads), so the call allocates nothing.  No counterpart in the reference (its decode takes
+ * a workspace buffer); it is for callers that cannot allocate device memory per call.
+ * Same arguments, semantics and errors as nvfp4kv_mla_decode, plus:
+ *   - NVFP4KV_EWORKSPACE if nvfp4kv_mla_decode_workspace_size() of the shape exceeds the
+ *     scratch (no shape does on a 148-SM device);
+ *   - the first call on a device looks up the scratch address with that device current;
+ *     make it before any stream capture begins;
+ *   - one scratch per device: calls whose kernels overlap on a device race on it.
+ */
+int nvfp4kv_mla_decode_static(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,
+                              const uint8_t* pool, int64_t pool_rows,
+                              const int32_t* tables, int64_t tables_stride,
+                              const int32_t* seq_lens,
+                              int batch, int q_len, int num_heads, int head_dim_qk, int kv_lora_rank,
+                              int sparse_topk, int page_size, int max_seq_len,
+                              float bmm1_scale, float bmm2_scale,
+                              void* out, int64_t out_stride_b, int64_t out_stride_q, int64_t out_stride_h,
+                              int32_t* err_flag, nvfp4kv_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
