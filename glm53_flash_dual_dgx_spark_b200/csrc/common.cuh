@@ -86,6 +86,15 @@ __device__ __forceinline__ void e2m1x8_to_f16x2x4(uint32_t codes, uint32_t (&h)[
         "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
         : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3]) : "r"(codes));
 }
+// One byte of two e2m1 codes (low nibble = element 0) -> f16x2 (low half = element 0).
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
+    uint32_t r;
+    asm("{\n\t.reg .b8 b0;\n\t"
+        "cvt.u8.u32 b0, %1;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t}"
+        : "=r"(r) : "r"(byte));
+    return r;
+}
 __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
     uint32_t r;
     asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
@@ -146,11 +155,11 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
+        // try_wait suspends the thread in hardware for a while when the phase is incomplete,
+        // so polling it costs few issue slots and wakes as soon as the phase completes.
 #pragma unroll 1
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 32; ++i)
             if (mbar_try_wait(bar, parity)) return true;
-            __nanosleep(32);   // yield issue slots to the warps doing work on this sub-partition
-        }
         if (*abort_flag) return false;
         if (globaltimer_ns() - t0 > NVFP4KV_WAIT_TIMEOUT_NS) {
             *abort_flag = 1;
@@ -243,6 +252,30 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
           "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+          "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]),
+          "r"(r[14]), "r"(r[15])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -267,6 +300,78 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
     d |= static_cast<uint64_t>(1) << 46;   // version
     d |= static_cast<uint64_t>(2) << 61;   // SWIZZLE_128B
     return d;
+}
+
+// D[tmem] (+)= A[smem] * B[smem] with NVFP4 operands: e2m1 codes (two per byte, element 0 in
+// the low nibble) and one ue4m3 scale per 16 K-elements for every row of A and of B, read
+// from TMEM at `sfa` / `sfb` (the MMA for K-chunk kk uses 4 columns: column q, lane 32p + r
+// of every sub-partition p holds the 4 scale bytes of row 32q + r).  K = 64 per instruction.
+__device__ __forceinline__ void tc_mma_fp4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                           uint32_t idesc, uint32_t accumulate, uint32_t sfa,
+                                           uint32_t sfb) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+
+// One elected lane of a converged warp returns true.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .b32 rx;\n\t.reg .pred px;\n\t"
+        "elect.sync rx|px, %1;\n\t"
+        "@px mov.s32 %0, 1;\n\t}"
+        : "+r"(pred)
+        : "r"(0xFFFFFFFFu));
+    return pred != 0;
+}
+
+// 2-D tiled TMA load of box (x, y) of `tmap` into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst_smem, const void* tmap, int x, int y,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst_smem), "l"(tmap), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// Bulk copy shared -> global (16-byte aligned, bytes % 16 == 0), tracked by bulk groups.
+__device__ __forceinline__ void bulk_copy_s2g(void* dst, uint32_t src_smem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                 ::"l"(dst), "r"(src_smem), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until every committed bulk group has finished reading its shared-memory source.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Two fp32 -> two e2m1 codes, round to nearest even, saturating at +-6:
+// returns lo_code | hi_code << 4.
+__device__ __forceinline__ uint32_t f32x2_to_e2m1x2(float lo, float hi) {
+    uint16_t v;
+    asm("{\n\t.reg .b8 q;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 q, %1, %2;\n\t"
+        "cvt.u16.u8 %0, q;\n\t}"
+        : "=h"(v)
+        : "f"(hi), "f"(lo));
+    return v;
+}
+
+// Instruction descriptor for kind::mxf4nvf4 (e2m1 A/B, ue4m3 scales per 16, fp32 D), K-major.
+__host__ __device__ constexpr uint32_t idesc_fp4_f32(int M, int N) {
+    return (1u << 7) | (1u << 10)                       // A, B format: e2m1
+           | (static_cast<uint32_t>(N >> 3) << 17)
+           | (static_cast<uint32_t>(M >> 4) << 24);     // bit 23 = 0: ue4m3 scales
 }
 
 // Instruction descriptor for kind::f16 with fp16 A/B and fp32 D.

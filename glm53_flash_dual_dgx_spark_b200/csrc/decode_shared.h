@@ -1,0 +1,50 @@
+// Pieces shared by the fused-decode kernels: the split plan, the validated call arguments
+// and the launchers each kernel file provides.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace nvfp4kv {
+
+constexpr int kDecTile = 128;       // tokens per tile
+constexpr int kDecRows = 64;        // query rows per CTA (one "group")
+constexpr int kDecMaxSplits = 64;   // split-K partitions per group
+
+// Bytes of one query group's prepared Q (dense path): the four NVFP4 terms as the fused
+// kernel's shared-memory image (64 KB), their scales (8 KB) and 64 per-row score factors.
+constexpr size_t kQImageBytes = 65536 + 8192 + 256;
+
+struct DecodePlan {
+    int groups, splits, tokens_per_split;
+    size_t part_bytes;   // splits * batch * groups * 64 * (512 + 2) floats when splits > 1, else 0
+    size_t qimg_bytes;   // batch * groups * kQImageBytes on the dense path, else 0
+    size_t ws_bytes;     // part_bytes + qimg_bytes
+};
+DecodePlan make_decode_plan(int batch, int q_len, int num_heads, int max_seq_len, int sparse_topk);
+
+// Arguments of nvfp4kv_mla_decode after validation.
+struct DecodeArgs {
+    const void* q;
+    int64_t q_sb, q_sq, q_sh;
+    const uint8_t* pool;
+    int64_t pool_rows;
+    const int32_t* tables;
+    int64_t tables_stride;
+    const int32_t* seq_lens;
+    int batch, q_len, num_heads;
+    int sparse_topk, page_size, page_shift, max_seq_len;
+    float bmm1_scale, bmm2_scale;
+    void* out;
+    int64_t o_sb, o_sq, o_sh;
+    float* part_o;    // [splits][batch][groups][64][512] when splits > 1
+    float* part_ml;   // [splits][batch][groups][64][2]
+    uint8_t* qimg;    // [batch][groups][kQImageBytes] (dense path)
+    int32_t* err;
+};
+
+// Dense (paged) decode with the QK^T product on the block-scaled fp4 tensor-core path.
+int launch_decode_fp4_dense(const DecodeArgs& a, const DecodePlan& pl, cudaStream_t st);
+
+}  // namespace nvfp4kv

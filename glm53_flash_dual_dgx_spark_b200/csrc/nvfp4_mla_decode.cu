@@ -36,6 +36,7 @@
 
 #include "abi_common.h"
 #include "common.cuh"
+#include "decode_shared.h"
 
 namespace nvfp4kv {
 namespace {
@@ -631,30 +632,7 @@ combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_
     *reinterpret_cast<uint2*>(out + b * o_sb + qi * o_sq + h * o_sh + 4 * threadIdx.x) = pk;
 }
 
-struct Plan {
-    int groups, splits, tokens_per_split;
-    size_t ws_bytes;
-};
-
-Plan make_plan(int batch, int q_len, int num_heads, int max_seq_len, int sparse_topk) {
-    Plan pl{};
-    pl.groups = (q_len * num_heads + kNQ - 1) / kNQ;
-    const int ctx = sparse_topk > 0 ? sparse_topk : max_seq_len;
-    const int tiles = ctx > 0 ? (ctx + kTile - 1) / kTile : 1;
-    const int units = batch * pl.groups;
-    const int sms = device_sm_count();
-    int want = units >= sms ? 1 : sms / units;
-    want = want < 1 ? 1 : (want > kMaxSplits ? kMaxSplits : want);
-    want = want > tiles ? tiles : want;
-    const int tiles_per_split = (tiles + want - 1) / want;
-    pl.tokens_per_split = tiles_per_split * kTile;
-    pl.splits = (tiles + tiles_per_split - 1) / tiles_per_split;
-    if (pl.splits < 1) pl.splits = 1;
-    pl.ws_bytes = pl.splits > 1
-                      ? static_cast<size_t>(pl.splits) * units * kNQ * (kLatent + 2) * sizeof(float)
-                      : 0;
-    return pl;
-}
+using Plan = DecodePlan;
 
 template <bool kSparse>
 int ensure_smem_attr() {
@@ -672,6 +650,29 @@ int ensure_smem_attr() {
 }
 
 }  // namespace
+
+DecodePlan make_decode_plan(int batch, int q_len, int num_heads, int max_seq_len, int sparse_topk) {
+    DecodePlan pl{};
+    pl.groups = (q_len * num_heads + kNQ - 1) / kNQ;
+    const int ctx = sparse_topk > 0 ? sparse_topk : max_seq_len;
+    const int tiles = ctx > 0 ? (ctx + kTile - 1) / kTile : 1;
+    const int units = batch * pl.groups;
+    const int sms = device_sm_count();
+    int want = units >= sms ? 1 : sms / units;
+    want = want < 1 ? 1 : (want > kMaxSplits ? kMaxSplits : want);
+    want = want > tiles ? tiles : want;
+    const int tiles_per_split = (tiles + want - 1) / want;
+    pl.tokens_per_split = tiles_per_split * kTile;
+    pl.splits = (tiles + tiles_per_split - 1) / tiles_per_split;
+    if (pl.splits < 1) pl.splits = 1;
+    pl.part_bytes = pl.splits > 1
+                        ? static_cast<size_t>(pl.splits) * units * kNQ * (kLatent + 2) * sizeof(float)
+                        : 0;
+    pl.qimg_bytes = sparse_topk > 0 ? 0 : static_cast<size_t>(units) * kQImageBytes;
+    pl.ws_bytes = pl.part_bytes + pl.qimg_bytes;
+    return pl;
+}
+
 }  // namespace nvfp4kv
 
 extern "C" int nvfp4kv_mla_decode_workspace_size(int batch, int q_len, int num_heads,
@@ -680,7 +681,7 @@ extern "C" int nvfp4kv_mla_decode_workspace_size(int batch, int q_len, int num_h
     if (!bytes) return fail(NVFP4KV_EINVAL, "workspace_size: null output");
     if (batch < 0 || q_len < 1 || num_heads < 1 || max_seq_len < 0 || sparse_topk < 0)
         return fail(NVFP4KV_EINVAL, "workspace_size: bad shape");
-    *bytes = batch == 0 ? 0 : make_plan(batch, q_len, num_heads, max_seq_len, sparse_topk).ws_bytes;
+    *bytes = batch == 0 ? 0 : make_decode_plan(batch, q_len, num_heads, max_seq_len, sparse_topk).ws_bytes;
     return NVFP4KV_OK;
 }
 
@@ -723,8 +724,8 @@ extern "C" int nvfp4kv_mla_decode(const void* q, int64_t q_stride_b, int64_t q_s
         return fail(NVFP4KV_EINVAL, "mla_decode: pool/q must be 16-byte aligned and q strides multiples of 8");
     if (reinterpret_cast<uintptr_t>(out) % 16 || out_stride_b % 8 || out_stride_q % 8 || out_stride_h % 8)
         return fail(NVFP4KV_EINVAL, "mla_decode: out must be 16-byte aligned and its strides multiples of 8");
-    const Plan pl = make_plan(batch, q_len, num_heads, max_seq_len, sparse_topk);
-    if (pl.splits > 1) {
+    const Plan pl = make_decode_plan(batch, q_len, num_heads, max_seq_len, sparse_topk);
+    if (pl.ws_bytes > 0) {
         if (!workspace || workspace_bytes < pl.ws_bytes)
             return fail(NVFP4KV_EWORKSPACE, "mla_decode: workspace %zu bytes < %zu required",
                         workspace_bytes, pl.ws_bytes);
@@ -759,11 +760,20 @@ extern "C" int nvfp4kv_mla_decode(const void* q, int64_t q_stride_b, int64_t q_s
     if (sparse_topk > 0) {
         if ((rc = ensure_smem_attr<true>()) != NVFP4KV_OK) return rc;
         mla_decode_kernel<true><<<grid, kThreads, kSmemBytes, st>>>(prm);
+        if ((rc = check_launch("nvfp4kv_mla_decode")) != NVFP4KV_OK) return rc;
     } else {
-        if ((rc = ensure_smem_attr<false>()) != NVFP4KV_OK) return rc;
-        mla_decode_kernel<false><<<grid, kThreads, kSmemBytes, st>>>(prm);
+        DecodeArgs a{};
+        a.q = q; a.q_sb = q_stride_b; a.q_sq = q_stride_q; a.q_sh = q_stride_h;
+        a.pool = pool; a.pool_rows = pool_rows;
+        a.tables = tables; a.tables_stride = tables_stride; a.seq_lens = seq_lens;
+        a.batch = batch; a.q_len = q_len; a.num_heads = num_heads;
+        a.sparse_topk = 0; a.page_size = page_size; a.page_shift = page_shift; a.max_seq_len = max_seq_len;
+        a.bmm1_scale = bmm1_scale; a.bmm2_scale = bmm2_scale;
+        a.out = out; a.o_sb = out_stride_b; a.o_sq = out_stride_q; a.o_sh = out_stride_h;
+        a.part_o = prm.part_o; a.part_ml = prm.part_ml; a.err = err_flag;
+        a.qimg = static_cast<uint8_t*>(workspace) + pl.part_bytes;
+        if ((rc = launch_decode_fp4_dense(a, pl, st)) != NVFP4KV_OK) return rc;
     }
-    if ((rc = check_launch("nvfp4kv_mla_decode")) != NVFP4KV_OK) return rc;
     if (pl.splits > 1) {
         combine_kernel<<<batch * pl.groups * kNQ, 128, 0, st>>>(prm.part_o, prm.part_ml, pl.splits, batch,
                                                           pl.groups, q_len, num_heads, bmm2_scale,

@@ -1,0 +1,862 @@
+// Fused NVFP4 paged gather + MLA decode attention for sm_100a, with Q.K^T on the block-scaled
+// fp4 tensor-core path (tcgen05.mma kind::mxf4nvf4).
+//
+// The 288-byte pool rows already are NVFP4: 512 e2m1 codes plus one e4m3 scale per 16
+// latent dims.  So the tile of 128 rows goes into shared memory unchanged (TMA, 128-byte
+// swizzled) and is the A operand of the QK product, with its scales as the A scale factors.
+// Q is written as a sum of four NVFP4 terms (each term codes the residual of the previous
+// ones with its own per-16 scales, after a per-row power-of-two prescale); four terms leave a
+// relative error of about 5e-5 in q, below bf16's own rounding.  The terms sit on the MMA's N
+// side in two passes of N = 128 (terms 1|2, then 3|4 accumulated on top), so S^T needs only
+// 128 TMEM columns: column n holds term-1+3 of query row n, column 64+n term-2+4.
+//
+// PV stays exact: V (= the same latent rows) is dequantised to fp16 (code x scale is exact in
+// fp16) in 16-token chunks and multiplied with fp16 probabilities, latent dims on M:
+//   O^T[d, n] += V^T[d, t] P^T[t, n]      M = 128 dims (4 blocks), N = 64 query rows, K = 16.
+//
+// Work unit (one CTA): query group (b, g) of up to 64 rows (MTP token i, head h) x token split.
+// Warps: 0-3 softmax (thread = token of the tile = TMEM lane), 4 MMA issue, 5-8 producers
+// (lane 0 of warp 5 also issues the TMA loads).  Per 128-token tile i:
+//   TMA      3-slot ring of raw tiles: codes [2 x 128 rows x 128 B] swizzled + scales [128 x 32 B];
+//            pages missing or beyond the context load as out-of-range boxes (zeros).
+//   producers  V chunks of 16 tokens -> fp16 [8 d-atoms x 16 tokens x 128 B] (2 buffers).
+//   MMA      QK(i): 16 fp4 MMAs M128 N128 K64 -> S^T; PV(i-1): 8 chunks x 4 fp16 MMAs.
+//   softmax  S^T row t -> x = s * log2(e) * bmm1_scale, masked; the running max of each query
+//            row is raised only when some x exceeds it by more than 8 (a CTA vote), and then
+//            O^T is rescaled; p = 2^(x - m) in fp16 -> P^T row t (swizzled), row sums kept
+//            per thread and reduced once at the end.
+// Splits write partial O and (max, sum) per row; the combine kernel of the caller merges
+// them.  Every wait is bounded (common.cuh).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include <mutex>
+
+#include "abi_common.h"
+#include "common.cuh"
+#include "decode_shared.h"
+
+namespace nvfp4kv {
+namespace {
+
+constexpr int kTile = kDecTile;                   // 128 tokens: QK M
+constexpr int kNQ = kDecRows;                     // 64 query rows: PV N
+constexpr int kChunk = 16;                        // tokens per V chunk = PV K
+constexpr int kChunks = kTile / kChunk;           // 8
+constexpr int kSlots = 3;                         // raw-tile ring depth
+constexpr int kVBufs = 2;                         // V chunk buffers
+constexpr int kSoftmaxWarps = 8;                  // 2 per TMEM sub-partition, 32 query rows each
+constexpr int kMmaWarp = 8;
+constexpr int kProducerWarps = 4;                 // warps 9-12: V chunks
+constexpr int kTmaWarp = 13;                      // lane 0 issues every TMA / bulk load
+constexpr int kThreads = (kTmaWarp + 1) * 32;     // 448
+constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
+constexpr float kRescaleLog2 = 8.0f;
+
+// Shared memory map (offsets from a 1024-byte aligned base).
+constexpr int kCodeBytes = kTile * 256;               // 2 atom columns x [128 rows x 128 B]
+constexpr int kScaleBytes = kTile * 32;               // [128 rows x 32 B]
+constexpr int kSlotBytes = kCodeBytes + kScaleBytes;  // 36864
+constexpr int SM_STAGE = 0;
+constexpr int SM_QB = SM_STAGE + kSlots * kSlotBytes;     // Q terms: 2 passes x 2 atom columns x [128 x 128 B]
+constexpr int SM_VT = SM_QB + 2 * kCodeBytes;             // kVBufs x [8 d-atoms x 16 tokens x 128 B] fp16
+constexpr int kVtBytes = 8 * kChunk * 128;
+constexpr int SM_PT = SM_VT + kVBufs * kVtBytes;          // [128 tokens x 128 B] fp16 P^T
+constexpr int SM_M = SM_PT + kTile * 128;                 // 64 f32: running row max (log2 units)
+constexpr int SM_ALPHA = SM_M + 256;                      // 64 f32: rescale factors / epilogue 1/l
+constexpr int SM_QS = SM_ALPHA + 256;                     // 64 f32: log2e * bmm1_scale * 2^e_row
+constexpr int SM_LIM = SM_QS + 256;                       // 64 i32: visible positions < lim
+constexpr int SM_LSUM = SM_LIM + 256;                     // 64 f32: row sums
+constexpr int SM_RED = SM_LSUM + 256;                     // 4 sub-partitions x 64 f32
+constexpr int SM_ROWOFF = SM_RED + 4 * 64 * 4;            // 64 i64: output row offsets
+constexpr int SM_FLAGS = SM_ROWOFF + 64 * 8;              // [0] TMEM base, [1] abort
+constexpr int SM_BARS = SM_FLAGS + 16;
+enum {
+    B_FULL = 0,                    // [kSlots] raw tile landed (TMA transaction bytes)
+    B_FREE = B_FULL + kSlots,      // [kSlots] producers finished reading the slot
+    B_QKD = B_FREE + kSlots,       // [kSlots] QK finished reading the slot
+    B_SFA_FULL = B_QKD + kSlots,   // [2] pool scales of a tile written to TMEM
+    B_S_FULL = B_SFA_FULL + 2,     // S^T complete in TMEM
+    B_S_FREE,                      // softmax has S^T in registers
+    B_P_FULL,                      // P^T complete in shared memory
+    B_PV_DONE,                     // PV of a tile complete (O^T stable, P^T free)
+    B_V_FULL,                      // [kVBufs] V chunk written
+    B_V_EMPTY = B_V_FULL + kVBufs, // [kVBufs] PV finished reading the V chunk
+    B_Q = B_V_EMPTY + kVBufs,      // prepared Q landed (set-up)
+    kNumBars
+};
+constexpr int SM_IDX = SM_BARS + ((kNumBars * 8 + 15) / 16) * 16;
+constexpr int kMaxIdx = 768;                              // staged page ids of the split
+constexpr int SM_END = SM_IDX + kMaxIdx * 4;
+constexpr int kSmemBytes = SM_END + 1024;                 // slack to align the base
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+static_assert(SM_VT >= kNQ * kLatent * 4, "epilogue staging fits below the V buffers");
+static_assert(kQImageBytes == 2 * kCodeBytes + 2 * 4096 + 256, "prepared-Q image layout");
+
+// Tensor memory columns (all 128 lanes).
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTS = 0;      // S^T: 128 columns
+constexpr uint32_t kTO = 128;    // O^T: 4 d-blocks x 64 rows
+constexpr uint32_t kTSFA = 384;  // 2 slots x 32 columns: pool scales of a tile
+constexpr uint32_t kTSFB = 448;  // 2 passes x 32 columns: Q-term scales
+
+struct Fp4Params {
+    const int32_t* tables;
+    int64_t tables_stride;
+    const int32_t* seq_lens;
+    int batch, q_len, num_heads, groups, splits;
+    int page_shift, box_rows;
+    int64_t num_pages;
+    int max_seq_len, tokens_per_split;
+    float bmm2_scale;
+    __nv_bfloat16* out;
+    int64_t o_sb, o_sq, o_sh;
+    float* part_o;
+    float* part_ml;
+    const uint8_t* qimg;
+    int32_t* err;
+};
+
+struct QPrepParams {
+    const __nv_bfloat16* q;
+    int64_t q_sb, q_sq, q_sh;
+    int q_len, num_heads, groups;
+    float scale_log2;
+    uint8_t* qimg;
+};
+
+// Q of one query group (64 rows) -> four NVFP4 terms, written as the fused kernel's shared
+// memory image: term tt goes to pass tt>>1, B-operand row 64 (tt&1) + n (K-major, 128-byte
+// swizzle); its per-16 e4m3 scales to [pass][row][32]; qs[n] = log2e * bmm1_scale * 2^e_n.
+// Each row is first scaled by 2^-e_n (exact) so its largest |q| lies in [2^10, 2^11) and the
+// first term's scales stay within e4m3; each later term codes the residual of the earlier
+// ones.  One warp per row, one lane per 16-dim block; grid = groups x 8 blocks of 8 rows.
+__global__ void __launch_bounds__(256) q_prep_kernel(const QPrepParams p) {
+    const int unit = blockIdx.x >> 3;
+    const int b = unit / p.groups, g = unit % p.groups;
+    const int lane = threadIdx.x & 31;
+    const int n = ((blockIdx.x & 7) << 3) | (threadIdx.x >> 5);
+    const int rows_here = min(kNQ, p.q_len * p.num_heads - g * kNQ);
+    const bool real = n < rows_here;
+    const int r = g * kNQ + n;
+    const int qi = real ? r / p.num_heads : 0, h = real ? r % p.num_heads : 0;
+    uint4 u0 = make_uint4(0, 0, 0, 0), u1 = make_uint4(0, 0, 0, 0);
+    if (real) {
+        const __nv_bfloat16* src = p.q + b * p.q_sb + qi * p.q_sq + h * p.q_sh + 16 * lane;
+        u0 = ldg_nc_v4(src);
+        u1 = ldg_nc_v4(src + 8);
+    }
+    const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    float x[16];
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        x[2 * j] = __uint_as_float(w8[j] << 16);
+        x[2 * j + 1] = __uint_as_float(w8[j] & 0xFFFF0000u);
+        amax = fmaxf(amax, fmaxf(fabsf(x[2 * j]), fabsf(x[2 * j + 1])));
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
+    int e = (amax > 0.0f && amax <= 3.0e38f) ? ilogbf(amax) - 10 : 0;
+    e = max(-100, min(100, e));
+    const float mul = ldexpf(1.0f, -e);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] *= mul;
+    uint8_t* img = p.qimg + static_cast<size_t>(unit) * kQImageBytes;
+    const int chunk = (lane & 15) >> 1;
+#pragma unroll
+    for (int tt = 0; tt < 4; ++tt) {
+        float am = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) am = fmaxf(am, fabsf(x[j]));
+        const uint8_t sb = am > 0.0f ? f32_to_e4m3(am / 6.0f) : static_cast<uint8_t>(0);
+        const float sf = e4m3_to_f32(sb);
+        const float inv = sf > 0.0f ? 1.0f / sf : 0.0f;
+        uint32_t wlo = 0, whi = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t byte = f32x2_to_e2m1x2(x[2 * j] * inv, x[2 * j + 1] * inv);
+            if (j < 4) wlo |= byte << (8 * j);
+            else whi |= byte << (8 * (j - 4));
+            const uint32_t dqw = e2m1x2_to_f16x2(byte);
+            x[2 * j] -= __half2float(__ushort_as_half(static_cast<unsigned short>(dqw & 0xFFFFu))) * sf;
+            x[2 * j + 1] -= __half2float(__ushort_as_half(static_cast<unsigned short>(dqw >> 16))) * sf;
+        }
+        const int ps = tt >> 1, R = 64 * (tt & 1) + n;
+        uint8_t* dst = img + ps * (2 * 16384) + (lane >> 4) * 16384 + (R >> 3) * 1024 + (R & 7) * 128 +
+                       ((chunk ^ (R & 7)) << 4) + 8 * (lane & 1);
+        *reinterpret_cast<uint2*>(dst) = make_uint2(wlo, whi);
+        img[2 * kCodeBytes + ps * 4096 + R * 32 + lane] = sb;
+    }
+    if (lane == 0)
+        reinterpret_cast<float*>(img + 2 * kCodeBytes + 2 * 4096)[n] = real ? p.scale_log2 * ldexpf(1.0f, e) : 0.0f;
+}
+
+__device__ __forceinline__ int page_id(const Fp4Params& p, const int* sidx, bool staged, int idx_base,
+                                       int b, int pos) {
+    const int pi = pos >> p.page_shift;
+    return staged ? sidx[pi - idx_base] : __ldg(p.tables + b * p.tables_stride + pi);
+}
+
+// TMA loads of tile `tile_start` into ring slot `slot`.  Every box is issued (a missing page
+// or a box past the context is addressed out of range and reads as zeros), so the slot always
+// receives kSlotBytes.
+__device__ __forceinline__ void load_tile(const Fp4Params& p, const void* tm_codes, const void* tm_scales,
+                                          uint32_t sbase, uint32_t bar_full, const int* sidx, bool staged,
+                                          int idx_base, int b, int tile_start, int end, int slot) {
+    mbar_arrive_expect_tx(bar_full, kSlotBytes);
+    const int box = p.box_rows;
+    const uint32_t codes = sbase + SM_STAGE + slot * kSlotBytes;
+    const uint32_t scales = codes + kCodeBytes;
+#pragma unroll 1
+    for (int r0 = 0; r0 < kTile; r0 += box) {
+        const int pos = tile_start + r0;
+        int y = -box;
+        if (pos < end) {
+            const int pg = page_id(p, sidx, staged, idx_base, b, pos);
+            if (pg >= 0 && pg < p.num_pages)
+                y = (pg << p.page_shift) | (pos & ((1 << p.page_shift) - 1));
+            else
+                set_error(p.err, NVFP4KV_DEVERR_BAD_PAGE);
+        }
+        tma_load_2d(codes + r0 * 128, tm_codes, 0, y, bar_full);
+        tma_load_2d(codes + 16384 + r0 * 128, tm_codes, 128, y, bar_full);
+        tma_load_2d(scales + r0 * 32, tm_scales, 256, y, bar_full);
+    }
+}
+
+// Pool scales of the tile in `slot` -> TMEM scale-factor columns `col` of this warp's
+// sub-partition: column 4kk+q of lane r holds the 4 scales (dims 64kk..64kk+63) of token
+// 32q + r.  Every sub-partition needs a full copy.
+__device__ __forceinline__ void scales_to_tmem(const uint8_t* scales, uint32_t taddr, int lane) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {   // columns 16 half .. +16: dims 256 half .. +256
+        uint32_t rr[16];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+            const uint4 w = reinterpret_cast<const uint4*>(scales + (32 * q4 + lane) * 32)[half];
+            rr[0 + q4] = w.x;
+            rr[4 + q4] = w.y;
+            rr[8 + q4] = w.z;
+            rr[12 + q4] = w.w;
+        }
+        tmem_st16(taddr + 16 * half, rr);
+    }
+    tmem_wait_st();
+}
+
+// Max (kSum = false) or sum over the 32 lanes of 32 values per lane; lane L returns the
+// result for value index L.  `v` is left unchanged: the first exchange step writes into a
+// 16-value scratch, which later steps halve in place.
+template <bool kSum>
+__device__ __forceinline__ float warp_reduce_scatter32(const float (&v)[32], int lane) {
+    float w[16];
+    {
+        const bool upper = (lane & 16) != 0;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const float send = upper ? v[j] : v[j + 16];
+            const float keep = upper ? v[j + 16] : v[j];
+            const float recv = __shfl_xor_sync(0xFFFFFFFFu, send, 16);
+            w[j] = kSum ? keep + recv : fmaxf(keep, recv);
+        }
+    }
+#pragma unroll
+    for (int off = 8; off >= 1; off >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int j = 0; j < off; ++j) {
+            const float send = upper ? w[j] : w[j + off];
+            const float keep = upper ? w[j + off] : w[j];
+            const float recv = __shfl_xor_sync(0xFFFFFFFFu, send, off);
+            w[j] = kSum ? keep + recv : fmaxf(keep, recv);
+        }
+    }
+    return w[0];
+}
+
+// Max over the 32 lanes of 16 values per lane; lane L returns the result for value L & 15.
+__device__ __forceinline__ float warp_max_scatter16(const float (&v)[16], int lane) {
+    float w[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) w[j] = fmaxf(v[j], __shfl_xor_sync(0xFFFFFFFFu, v[j], 16));
+#pragma unroll
+    for (int off = 8; off >= 1; off >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int j = 0; j < off; ++j) {
+            const float send = upper ? w[j] : w[j + off];
+            const float keep = upper ? w[j + off] : w[j];
+            w[j] = fmaxf(keep, __shfl_xor_sync(0xFFFFFFFFu, send, off));
+        }
+    }
+    return w[0];
+}
+
+// p = 2^(s qs - m) for the 32 rows of this thread (0 where not visible), packed as fp16 pairs;
+// row sums accumulate in l.
+__device__ __forceinline__ void probs32(const float (&sraw)[32], const float* qs_h, const float* M_h,
+                                        const int* lim_h, bool tok_ok, bool per_row_lim, int pos,
+                                        float (&l)[32], uint32_t (&pk)[16]) {
+#pragma unroll
+    for (int n4 = 0; n4 < 8; ++n4) {
+        const float4 q4 = reinterpret_cast<const float4*>(qs_h)[n4];
+        const float4 m4 = reinterpret_cast<const float4*>(M_h)[n4];
+        const int4 l4 = reinterpret_cast<const int4*>(lim_h)[n4];
+        const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+        const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
+        const int lv[4] = {l4.x, l4.y, l4.z, l4.w};
+        float pv[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const bool vis = tok_ok && (!per_row_lim || pos < lv[k]);
+            pv[k] = vis ? ex2_approx(fmaf(sraw[4 * n4 + k], qv[k], -mv[k])) : 0.0f;
+            l[4 * n4 + k] += pv[k];
+        }
+        pk[2 * n4] = pack_half2(pv[0], pv[1]);
+        pk[2 * n4 + 1] = pack_half2(pv[2], pv[3]);
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+decode_fp4_dense_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ CUtensorMap tm_codes,
+                        const __grid_constant__ CUtensorMap tm_scales) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    const uint32_t sbase = smem_u32(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const int s = blockIdx.x % p.splits;
+    const int bg = blockIdx.x / p.splits;
+    const int g = bg % p.groups;
+    const int b = bg / p.groups;
+
+    int L = __ldg(p.seq_lens + b);
+    if (L > p.max_seq_len) {
+        if (threadIdx.x == 0) set_error(p.err, NVFP4KV_DEVERR_SEQ_LEN);
+        L = p.max_seq_len;
+    }
+    if (L < 0) L = 0;
+    const int start = s * p.tokens_per_split;
+    const int end = min(start + p.tokens_per_split, L);
+    const int n_tiles = end > start ? (end - start + kTile - 1) / kTile : 0;
+    const int rows_here = min(kNQ, p.q_len * p.num_heads - g * kNQ);
+
+    float* Mrow = reinterpret_cast<float*>(smem + SM_M);
+    float* alpha = reinterpret_cast<float*>(smem + SM_ALPHA);
+    float* qs = reinterpret_cast<float*>(smem + SM_QS);
+    int* lim = reinterpret_cast<int*>(smem + SM_LIM);
+    float* lsum = reinterpret_cast<float*>(smem + SM_LSUM);
+    float* red = reinterpret_cast<float*>(smem + SM_RED);
+    int64_t* rowoff = reinterpret_cast<int64_t*>(smem + SM_ROWOFF);
+    int* sidx = reinterpret_cast<int*>(smem + SM_IDX);
+    volatile int* flags = reinterpret_cast<volatile int*>(smem + SM_FLAGS);
+    volatile int* abort_flag = flags + 1;
+    auto bar = [&](int i) -> uint32_t { return sbase + SM_BARS + 8 * i; };
+
+    if (threadIdx.x == 0) {
+        for (int k = 0; k < kSlots; ++k) {
+            mbar_init(bar(B_FULL + k), 1);
+            mbar_init(bar(B_FREE + k), kProducerWarps);
+            mbar_init(bar(B_QKD + k), 1);
+        }
+        for (int k = 0; k < 2; ++k) mbar_init(bar(B_SFA_FULL + k), 4);
+        for (int k = 0; k < kVBufs; ++k) {
+            mbar_init(bar(B_V_FULL + k), kProducerWarps);
+            mbar_init(bar(B_V_EMPTY + k), 1);
+        }
+        mbar_init(bar(B_S_FULL), 1);
+        mbar_init(bar(B_S_FREE), kSoftmaxWarps);
+        mbar_init(bar(B_P_FULL), kSoftmaxWarps);
+        mbar_init(bar(B_PV_DONE), 1);
+        mbar_init(bar(B_Q), 1);
+        flags[1] = 0;
+        mbar_fence_init();
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc(sbase + SM_FLAGS, kTmemCols);
+        tmem_relinquish();
+    }
+    // page ids of this split
+    const int idx_base = start >> p.page_shift;
+    const int idx_count = end > start ? ((end - 1) >> p.page_shift) - idx_base + 1 : 0;
+    const bool staged = idx_count <= kMaxIdx;
+    if (staged)
+        for (int k = threadIdx.x; k < idx_count; k += kThreads)
+            sidx[k] = __ldg(p.tables + b * p.tables_stride + idx_base + k);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = static_cast<uint32_t>(flags[0]);
+
+    if (warp == kTmaWarp) {
+        // ============================================================ TMA / bulk loads
+        if (lane == 0) {
+            const uint8_t* img = p.qimg + static_cast<size_t>(b * p.groups + g) * kQImageBytes;
+            mbar_arrive_expect_tx(bar(B_Q), static_cast<uint32_t>(kQImageBytes));
+            bulk_copy_g2s(sbase + SM_QB, img, 2 * kCodeBytes, bar(B_Q));
+            bulk_copy_g2s(sbase + SM_PT, img + 2 * kCodeBytes, 2 * 4096, bar(B_Q));
+            bulk_copy_g2s(sbase + SM_QS, img + 2 * kCodeBytes + 2 * 4096, 256, bar(B_Q));
+            tma_prefetch_desc(&tm_codes);
+            tma_prefetch_desc(&tm_scales);
+            for (int j = 0; j < kSlots && j < n_tiles; ++j)
+                load_tile(p, &tm_codes, &tm_scales, sbase, bar(B_FULL + j), sidx, staged, idx_base, b,
+                          start + j * kTile, end, j);
+#pragma unroll 1
+            for (int i = 0; i + kSlots < n_tiles; ++i) {
+                const int slot = i % kSlots;
+                const uint32_t sph = (i / kSlots) & 1;
+                mbar_wait(bar(B_FREE + slot), sph, abort_flag, p.err);
+                mbar_wait(bar(B_QKD + slot), sph, abort_flag, p.err);
+                fence_proxy_async_smem();
+                load_tile(p, &tm_codes, &tm_scales, sbase, bar(B_FULL + slot), sidx, staged, idx_base, b,
+                          start + (i + kSlots) * kTile, end, slot);
+            }
+        }
+        __syncwarp();
+    } else if (warp == kMmaWarp) {
+        // ============================================================ MMA issue
+        constexpr uint32_t idq = idesc_fp4_f32(kTile, 128);
+        constexpr uint32_t idp = idesc_f16_f32(128, kNQ, true, true);
+        const uint64_t dq0 = smem_desc_sw128(sbase + SM_QB, 16, 1024);
+        const uint64_t dpt = smem_desc_sw128(sbase + SM_PT, 16, 1024);
+        mbar_wait(bar(B_Q), 0, abort_flag, p.err);   // Q-term codes in shared memory
+#pragma unroll 1
+        for (int i = 0; i <= n_tiles; ++i) {
+            if (i < n_tiles) {
+                const int slot = i % kSlots, fb = i & 1;
+                mbar_wait(bar(B_FULL + slot), (i / kSlots) & 1, abort_flag, p.err);
+                mbar_wait(bar(B_SFA_FULL + fb), (i >> 1) & 1, abort_flag, p.err);
+                if (i > 0) mbar_wait(bar(B_S_FREE), (i - 1) & 1, abort_flag, p.err);
+                tc_fence_after();
+                const uint64_t da0 = smem_desc_sw128(sbase + SM_STAGE + slot * kSlotBytes, 16, 1024);
+                const uint32_t sfa = tmem + kTSFA + 32 * fb, sfb = tmem + kTSFB;
+                if (elect_one()) {
+#pragma unroll
+                    for (int ps = 0; ps < 2; ++ps)
+#pragma unroll
+                        for (int kk = 0; kk < 8; ++kk) {
+                            const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+                            tc_mma_fp4(tmem + kTS, da0 + off, dq0 + ((ps * 32768) >> 4) + off, idq,
+                                       (ps | kk) != 0, sfa + 4 * kk, sfb + 32 * ps + 4 * kk);
+                        }
+                    tc_commit(bar(B_S_FULL));
+                    tc_commit(bar(B_QKD + slot));
+                }
+                __syncwarp();
+            }
+            if (i > 0) {
+                const int t = i - 1;
+                mbar_wait(bar(B_P_FULL), t & 1, abort_flag, p.err);
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < kChunks; ++c) {
+                    const int u = kChunks * t + c, vb = u % kVBufs;
+                    mbar_wait(bar(B_V_FULL + vb), (u / kVBufs) & 1, abort_flag, p.err);
+                    tc_fence_after();
+                    const uint64_t dv = smem_desc_sw128(sbase + SM_VT + vb * kVtBytes, 2048, 1024);
+                    const uint64_t dp = dpt + ((c * kChunk * 128) >> 4);
+                    if (elect_one()) {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            tc_mma_f16(tmem + kTO + 64 * j, dv + ((j * 4096) >> 4), dp, idp, (t | c) != 0);
+                        tc_commit(bar(B_V_EMPTY + vb));
+                        if (c == kChunks - 1) tc_commit(bar(B_PV_DONE));
+                    }
+                    __syncwarp();
+                }
+            }
+        }
+    } else if (warp > kMmaWarp) {
+        // ============================================================ producers: V chunks
+        // lane -> token tq = lane & 15 of the chunk; 16-byte code chunks (32 dims) sc0 =
+        // 4 pw + (lane >> 4) and sc0 + 2
+        const int pw = warp - kMmaWarp - 1;
+#pragma unroll 1
+        for (int i = 0; i < n_tiles; ++i) {
+            const int slot = i % kSlots;
+            mbar_wait(bar(B_FULL + slot), (i / kSlots) & 1, abort_flag, p.err);
+            const uint8_t* codes = smem + SM_STAGE + slot * kSlotBytes;
+            const uint8_t* scales = codes + kCodeBytes;
+#pragma unroll 1
+            for (int c = 0; c < kChunks; ++c) {
+                const int u = kChunks * i + c, vb = u % kVBufs;
+                const int tq = lane & 15;
+                const int tok = c * kChunk + tq;
+                const int sc0 = 4 * pw + (lane >> 4);
+                // dequantise both 32-dim pieces into registers first; the destination buffer
+                // is awaited only for the stores
+                uint32_t hv[2][16];
+#pragma unroll
+                for (int it = 0; it < 2; ++it) {
+                    const int sc = sc0 + 2 * it;
+                    const uint4 cw = *reinterpret_cast<const uint4*>(
+                        codes + (sc >> 3) * 16384 + (tok >> 3) * 1024 + (tok & 7) * 128 + (((sc & 7) ^ (tok & 7)) << 4));
+                    const uint32_t s2 = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(scales + tok * 32 + 2 * sc));
+                    const uint32_t slo = (s2 & 0xFFFFu) * 0x10001u, shi = (s2 >> 16) * 0x10001u;
+                    const uint32_t cws[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) {
+                        uint32_t t4[4];
+                        e2m1x8_to_f16x2x4(cws[w], t4);
+                        const uint32_t sv = w < 2 ? slo : shi;
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) hv[it][4 * w + k] = hmul2_u32(t4[k], sv);
+                    }
+                }
+                if (u >= kVBufs) mbar_wait(bar(B_V_EMPTY + vb), ((u / kVBufs) - 1) & 1, abort_flag, p.err);
+                uint8_t* vt = smem + SM_VT + vb * kVtBytes + tq * 128;
+#pragma unroll
+                for (int it = 0; it < 2; ++it) {
+                    const int sc = sc0 + 2 * it;
+                    // dims 32sc + 8j .. +8 -> d-atom sc>>1, 16-byte chunk 4(sc&1) + j
+                    uint8_t* row = vt + (sc >> 1) * 2048;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        *reinterpret_cast<uint4*>(row + (((4 * (sc & 1) + j) ^ (tq & 7)) << 4)) =
+                            make_uint4(hv[it][4 * j], hv[it][4 * j + 1], hv[it][4 * j + 2], hv[it][4 * j + 3]);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(B_V_FULL + vb));
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_FREE + slot));
+        }
+    } else {
+        // ============================================================ softmax
+        // warp w: TMEM sub-partition sp = w & 3 (token t = 32 sp + lane), query rows 32 hh .. +32
+        const int sp = warp & 3, hh = warp >> 2;
+        const int t = 32 * sp + lane;
+        const uint32_t lane_base = static_cast<uint32_t>(32 * sp) << 16;
+        const float* qs_h = qs + 32 * hh;
+        const int* lim_h = lim + 32 * hh;
+        const float* M_h = Mrow + 32 * hh;
+        const float* alpha_h = alpha + 32 * hh;
+        const bool per_row_lim = p.q_len > 1;   // q_len 1: every row sees the whole context
+
+        // ---- set-up: per-row constants, Q-term scales (B scale factors) and tile 0's pool
+        // scales (A scale factors) into TMEM; every sub-partition gets a full copy
+        mbar_wait(bar(B_Q), 0, abort_flag, p.err);
+        if (threadIdx.x < kNQ) {
+            const int n = threadIdx.x;
+            const bool real = n < rows_here;
+            const int r = g * kNQ + n;
+            const int qi = real ? r / p.num_heads : 0, h = real ? r % p.num_heads : 0;
+            lim[n] = real ? L - (p.q_len - 1 - qi) : -1;
+            rowoff[n] = real ? b * p.o_sb + qi * p.o_sq + h * p.o_sh : 0;
+            Mrow[n] = -INFINITY;
+        }
+        {
+            const uint8_t* sfb_img = smem + SM_PT;   // [2 passes][128 rows][32 scale bytes]
+            uint32_t rr[32];
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4)
+                    rr[4 * kk + q4] = *reinterpret_cast<const uint32_t*>(sfb_img + hh * 4096 +
+                                                                         (32 * q4 + lane) * 32 + 4 * kk);
+            tmem_st32(tmem + kTSFB + 32 * hh + lane_base, rr);
+            tmem_wait_st();
+        }
+        if (hh == 0 && n_tiles > 0) {
+            mbar_wait(bar(B_FULL + 0), 0, abort_flag, p.err);
+            scales_to_tmem(smem + SM_STAGE + kCodeBytes, tmem + kTSFA + lane_base, lane);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_SFA_FULL + 0));
+        }
+        named_bar_sync(1, kSoftmaxThreads);   // per-row constants visible; the SFB image is read
+
+        float l[32];
+#pragma unroll
+        for (int n = 0; n < 32; ++n) l[n] = 0.0f;
+#pragma unroll 1
+        for (int i = 0; i < n_tiles; ++i) {
+            mbar_wait(bar(B_S_FULL), i & 1, abort_flag, p.err);
+            tc_fence_after();
+            // pool scales of tile i+1 -> its TMEM slot (QK(i-1), the slot's last reader, is
+            // complete: S_FULL(i) tracks every earlier MMA)
+            if (hh == 0 && i + 1 < n_tiles) {
+                const int slot1 = (i + 1) % kSlots;
+                mbar_wait(bar(B_FULL + slot1), ((i + 1) / kSlots) & 1, abort_flag, p.err);
+                scales_to_tmem(smem + SM_STAGE + slot1 * kSlotBytes + kCodeBytes,
+                               tmem + kTSFA + 32 * ((i + 1) & 1) + lane_base, lane);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(B_SFA_FULL + ((i + 1) & 1)));
+            }
+
+            float sraw[32];
+            {
+                uint32_t a[32], c2[32];
+                tmem_ld32(tmem + kTS + 32 * hh + lane_base, a);
+                tmem_ld32(tmem + kTS + 64 + 32 * hh + lane_base, c2);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) sraw[j] = __uint_as_float(a[j]) + __uint_as_float(c2[j]);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_S_FREE));
+            const int pos = start + i * kTile + t;
+            bool tok_ok = pos < end;
+            if (tok_ok) {
+                const int pg = page_id(p, sidx, staged, idx_base, b, pos);
+                tok_ok = pg >= 0 && pg < p.num_pages;
+            }
+            // does any visible score exceed its row's running max by more than 2^8?
+            bool grow = false;
+#pragma unroll
+            for (int n4 = 0; n4 < 8; ++n4) {
+                const float4 q4 = reinterpret_cast<const float4*>(qs_h)[n4];
+                const float4 m4 = reinterpret_cast<const float4*>(M_h)[n4];
+                const int4 l4 = reinterpret_cast<const int4*>(lim_h)[n4];
+                const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+                const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
+                const int lv[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const bool vis = tok_ok && (!per_row_lim || pos < lv[k]);
+                    grow |= vis && fmaf(sraw[4 * n4 + k], qv[k], -mv[k]) > kRescaleLog2;
+                }
+            }
+            const bool any = named_bar_red_or(1, kSoftmaxThreads, grow);
+            uint32_t pk[16];
+            if (any) {
+                // new row max = max(old, tile max); alpha = 2^(old - new)
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {   // 16 rows at a time keeps the register count down
+                    float xv[16];
+#pragma unroll
+                    for (int n4 = 0; n4 < 4; ++n4) {
+                        const float4 q4 = reinterpret_cast<const float4*>(qs_h + 16 * hf)[n4];
+                        const int4 l4 = reinterpret_cast<const int4*>(lim_h + 16 * hf)[n4];
+                        const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+                        const int lv[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const bool vis = tok_ok && (!per_row_lim || pos < lv[k]);
+                            xv[4 * n4 + k] = vis ? sraw[16 * hf + 4 * n4 + k] * qv[k] : -INFINITY;
+                        }
+                    }
+                    const float mx = warp_max_scatter16(xv, lane);
+                    if (lane < 16) red[sp * 64 + 32 * hh + 16 * hf + lane] = mx;
+                }
+                named_bar_sync(1, kSoftmaxThreads);
+                if (threadIdx.x < 64) {
+                    const int n = threadIdx.x;
+                    const float mo = Mrow[n];
+                    const float tmx = fmaxf(fmaxf(red[n], red[64 + n]), fmaxf(red[128 + n], red[192 + n]));
+                    const float mn = fmaxf(mo, tmx);
+                    alpha[n] = (mn == -INFINITY) ? 1.0f : ex2_approx(mo - mn);
+                    Mrow[n] = mn;
+                }
+                named_bar_sync(1, kSoftmaxThreads);
+#pragma unroll
+                for (int n4 = 0; n4 < 8; ++n4) {
+                    const float4 a4 = reinterpret_cast<const float4*>(alpha_h)[n4];
+                    l[4 * n4] *= a4.x;
+                    l[4 * n4 + 1] *= a4.y;
+                    l[4 * n4 + 2] *= a4.z;
+                    l[4 * n4 + 3] *= a4.w;
+                }
+            } else {
+                // common case: the maxima stand, so P is ready before PV(i-1) completes
+                probs32(sraw, qs_h, M_h, lim_h, tok_ok, per_row_lim, pos, l, pk);
+            }
+            if (i > 0) {
+                // P^T is single-buffered and O^T must be stable: wait for PV(i-1).  QK(i+1) is
+                // queued on the tensor core ahead of PV(i), so the work below stays hidden.
+                mbar_wait(bar(B_PV_DONE), (i - 1) & 1, abort_flag, p.err);
+                tc_fence_after();
+                if (any) {
+#pragma unroll 1
+                    for (int cc = 0; cc < 8; ++cc) {   // 16 columns at a time
+                        const int jh = 16 * (cc & 1);
+                        const uint32_t col = tmem + kTO + 64 * (cc >> 1) + 32 * hh + jh + lane_base;
+                        uint32_t o[16];
+                        tmem_ld16(col, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha_h[jh + j]);
+                        tmem_st16(col, o);
+                    }
+                    tmem_wait_st();
+                }
+            }
+            if (any) probs32(sraw, qs_h, M_h, lim_h, tok_ok, per_row_lim, pos, l, pk);
+            // P^T row t, 16-byte chunks 4hh .. 4hh+3 (rows 32hh .. 32hh+31), 128-byte swizzled
+            uint8_t* prow = smem + SM_PT + t * 128;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                *reinterpret_cast<uint4*>(prow + (((4 * hh + k) ^ (t & 7)) << 4)) =
+                    make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_P_FULL));
+        }
+
+        // ---- epilogue
+        if (n_tiles > 0) {
+            mbar_wait(bar(B_PV_DONE), (n_tiles - 1) & 1, abort_flag, p.err);
+            tc_fence_after();
+        }
+        red[sp * 64 + 32 * hh + lane] = warp_reduce_scatter32<true>(l, lane);
+        named_bar_sync(1, kSoftmaxThreads);
+        const bool final_out = p.splits == 1;
+        if (threadIdx.x < 64) {
+            const int n = threadIdx.x;
+            const float ls = red[n] + red[64 + n] + red[128 + n] + red[192 + n];
+            lsum[n] = ls;
+            alpha[n] = (n_tiles > 0 && ls > 0.0f) ? p.bmm2_scale / ls : 0.0f;
+        }
+        named_bar_sync(1, kSoftmaxThreads);
+        // O^T -> row-major staging at offset 0 (the ring and Q regions are idle now):
+        // warp (sp, hh) moves rows 32hh .. +32 of dims 128 jb + 32 sp + lane.
+#pragma unroll 1
+        for (int jb = 0; jb < 4; ++jb) {
+            uint32_t o[32];
+            if (n_tiles > 0) {
+                tmem_ld32(tmem + kTO + 64 * jb + 32 * hh + lane_base, o);
+                tmem_wait_ld();
+            } else {
+#pragma unroll
+                for (int k = 0; k < 32; ++k) o[k] = 0u;
+            }
+            const int d = 128 * jb + t;
+            if (final_out) {
+                __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem);
+#pragma unroll
+                for (int k = 0; k < 32; ++k) {
+                    const int n = 32 * hh + k;
+                    stg[n * kLatent + d] = __float2bfloat16_rn(__uint_as_float(o[k]) * alpha[n]);
+                }
+            } else {
+                float* stg = reinterpret_cast<float*>(smem);
+#pragma unroll
+                for (int k = 0; k < 32; ++k) stg[(32 * hh + k) * kLatent + d] = __uint_as_float(o[k]);
+            }
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(1, kSoftmaxThreads);
+        const int n = threadIdx.x;
+        if (n < rows_here) {
+            if (final_out) {
+                bulk_copy_s2g(p.out + rowoff[n], sbase + n * kLatent * 2, kLatent * 2);
+            } else {
+                const int64_t unit = (static_cast<int64_t>(s) * p.batch + b) * p.groups + g;
+                bulk_copy_s2g(p.part_o + (unit * kNQ + n) * kLatent, sbase + n * kLatent * 4, kLatent * 4);
+                float* ml = p.part_ml + (unit * kNQ + n) * 2;
+                ml[0] = Mrow[n];
+                ml[1] = lsum[n];
+            }
+            bulk_commit_group();
+            bulk_wait_group_read0();
+        } else if (!final_out && n < kNQ) {
+            const int64_t unit = (static_cast<int64_t>(s) * p.batch + b) * p.groups + g;
+            float* ml = p.part_ml + (unit * kNQ + n) * 2;
+            ml[0] = -INFINITY;
+            ml[1] = 0.0f;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+int make_pool_map(CUtensorMap* m, const uint8_t* pool, int64_t pool_rows, uint32_t box_x, uint32_t box_y,
+                  CUtensorMapSwizzle swz) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return fail(NVFP4KV_ECUDA, "mla_decode: cuTensorMapEncodeTiled is unavailable");
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kRowBytes), static_cast<cuuint64_t>(pool_rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kRowBytes)};
+    const cuuint32_t box[2] = {box_x, box_y};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(pool), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(NVFP4KV_ECUDA, "mla_decode: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return NVFP4KV_OK;
+}
+
+int ensure_fp4_smem_attr() {
+    static int done[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaGetDevice failed");
+    if (dev >= 0 && dev < 64 && done[dev]) return NVFP4KV_OK;
+    const cudaError_t e = cudaFuncSetAttribute(decode_fp4_dense_kernel,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess)
+        return fail(NVFP4KV_ECUDA, "cudaFuncSetAttribute(max dynamic smem %d): %s", kSmemBytes, cudaGetErrorString(e));
+    if (dev >= 0 && dev < 64) done[dev] = 1;
+    return NVFP4KV_OK;
+}
+
+}  // namespace
+
+int launch_decode_fp4_dense(const DecodeArgs& a, const DecodePlan& pl, cudaStream_t st) {
+    if (a.page_size < 16)
+        return fail(NVFP4KV_EINVAL, "mla_decode: page_size must be >= 16 (got %d)", a.page_size);
+    if (!a.qimg || reinterpret_cast<uintptr_t>(a.qimg) % 16)
+        return fail(NVFP4KV_EWORKSPACE, "mla_decode: no 16-byte aligned workspace for the prepared Q");
+    if (a.pool_rows > 0x7FFFFFFFll)
+        return fail(NVFP4KV_EINVAL, "mla_decode: pool_rows %lld beyond 2^31 - 1", static_cast<long long>(a.pool_rows));
+    const int box_rows = a.page_size < kTile ? a.page_size : kTile;
+    CUtensorMap tm_codes, tm_scales;
+    int rc;
+    if ((rc = make_pool_map(&tm_codes, a.pool, a.pool_rows, 128, box_rows, CU_TENSOR_MAP_SWIZZLE_128B)) != NVFP4KV_OK)
+        return rc;
+    if ((rc = make_pool_map(&tm_scales, a.pool, a.pool_rows, 32, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE)) != NVFP4KV_OK)
+        return rc;
+    if ((rc = ensure_fp4_smem_attr()) != NVFP4KV_OK) return rc;
+    QPrepParams qp{};
+    qp.q = static_cast<const __nv_bfloat16*>(a.q);
+    qp.q_sb = a.q_sb; qp.q_sq = a.q_sq; qp.q_sh = a.q_sh;
+    qp.q_len = a.q_len; qp.num_heads = a.num_heads; qp.groups = pl.groups;
+    qp.scale_log2 = a.bmm1_scale * 1.4426950408889634f;
+    qp.qimg = a.qimg;
+    q_prep_kernel<<<a.batch * pl.groups * 8, 256, 0, st>>>(qp);
+    if ((rc = check_launch("nvfp4kv_mla_decode (Q preparation)")) != NVFP4KV_OK) return rc;
+    Fp4Params p{};
+    p.tables = a.tables; p.tables_stride = a.tables_stride;
+    p.seq_lens = a.seq_lens;
+    p.batch = a.batch; p.q_len = a.q_len; p.num_heads = a.num_heads;
+    p.groups = pl.groups; p.splits = pl.splits;
+    p.page_shift = a.page_shift; p.box_rows = box_rows;
+    p.num_pages = a.pool_rows / a.page_size;
+    p.max_seq_len = a.max_seq_len;
+    p.tokens_per_split = pl.tokens_per_split;
+    p.bmm2_scale = a.bmm2_scale;
+    p.out = static_cast<__nv_bfloat16*>(a.out);
+    p.o_sb = a.o_sb; p.o_sq = a.o_sq; p.o_sh = a.o_sh;
+    p.part_o = a.part_o; p.part_ml = a.part_ml;
+    p.qimg = a.qimg;
+    p.err = a.err;
+    const dim3 grid(static_cast<unsigned>(a.batch * pl.groups * pl.splits));
+    decode_fp4_dense_kernel<<<grid, kThreads, kSmemBytes, st>>>(p, tm_codes, tm_scales);
+    return check_launch("nvfp4kv_mla_decode (fp4 dense)");
+}
+
+}  // namespace nvfp4kv

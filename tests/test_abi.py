@@ -77,11 +77,14 @@ def test_gather_and_decode_argument_checks_without_launch():
 def test_workspace_size_formula():
     lib = _lib.lib()
     out = ctypes.c_size_t()
+    qimg = 65536 + 8192 + 256                      # prepared Q of one 64-row query group (dense)
     assert lib.nvfp4kv_mla_decode_workspace_size(16, 1, 64, 8192, 0, ctypes.byref(out)) == _lib.OK
     # 16 query groups on (at least) 148 SMs: 8 splits of 8 tiles; 64 rows x (512 + 2) floats
-    assert out.value == 8 * 16 * 64 * 514 * 4
+    assert out.value == 8 * 16 * 64 * 514 * 4 + 16 * qimg
     assert lib.nvfp4kv_mla_decode_workspace_size(256, 1, 64, 8192, 0, ctypes.byref(out)) == _lib.OK
-    assert out.value == 0                          # enough query groups: no split, no workspace
+    assert out.value == 256 * qimg                 # enough query groups: no split partials
+    assert lib.nvfp4kv_mla_decode_workspace_size(16, 1, 64, 0, 2048, ctypes.byref(out)) == _lib.OK
+    assert out.value == 8 * 16 * 64 * 514 * 4     # sparse: 8 splits of 2 tiles, no prepared Q
     assert lib.nvfp4kv_mla_decode_workspace_size(-1, 1, 64, 8192, 0, ctypes.byref(out)) == _lib.EINVAL
 
 

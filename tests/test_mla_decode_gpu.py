@@ -34,7 +34,10 @@ def make_pool(num_pages, page=64, seed=0, scale=1.0, device="cuda"):
     return torch.from_numpy(pool).to(device).view(num_pages, page, 288), pool
 
 
-def check(out, ref, what=""):
+def check(out, ref, what="", errors_ok=0):
+    from glm53_flash_dual_dgx_spark_b200 import glm53_nvfp4_runtime as rt
+    err = rt.device_errors()
+    assert err & ~errors_ok == 0, f"{what}: device error bits {err:#x}"
     o = out.float().cpu().numpy()
     assert np.isfinite(o).all(), f"{what}: non-finite output"
     rel = np.linalg.norm(o - ref) / max(np.linalg.norm(ref), 1e-30)
@@ -87,6 +90,19 @@ def test_dense_peaked_softmax_rescales(rt):
     """Large logits make the running max move by far more than the lazy-rescale threshold."""
     out, ref = run_dense(rt, 2, 64, 1, [3000, 1024], qscale=8.0)
     check(out, ref, "peaked")
+
+
+def test_dense_many_tiles_per_split(rt):
+    """20 x 128 heads = 40 work units: 3 splits of 11 tiles each, so every CTA walks its raw-tile
+    ring several times over and carries O across tiles."""
+    out, ref = run_dense(rt, 20, 128, 1, [4000 - 97 * k for k in range(20)], num_pages=64)
+    check(out, ref, "many tiles")
+
+
+def test_dense_many_tiles_peaked(rt):
+    """Multi-tile CTAs with large logits: the running max moves across tiles and O^T is rescaled."""
+    out, ref = run_dense(rt, 20, 64, 1, [3000] * 10 + [2500] * 10, num_pages=48, qscale=8.0)
+    check(out, ref, "many tiles peaked")
 
 
 def test_dense_zero_length_and_bad_page(rt):
