@@ -304,8 +304,8 @@ def main() -> None:
             graphs.append(gr)
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
-    launches_per_step = 2 if rt.mla_decode_workspace_size(wl["B"], wl["QL"], wl["H"], wl["ctx"],
-                                                          wl["topk"], dev) > 0 else 1
+    splits, launches_per_step = rt.mla_decode_plan(wl["B"], wl["QL"], wl["H"], wl["topk"] or wl["ctx"],
+                                                    wl["topk"], dev)
 
     sampler = ClockSampler(local)
     sampler.start()
@@ -375,6 +375,21 @@ def main() -> None:
         dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
     e2e_value = kvb * e2e_steps * world / (float(e_ms.item()) / 1e3) / 1e9
 
+    # ---- the attention kernel alone: CUDA events recorded by the library immediately around
+    # it (on its stream), over a separate run of the same steps
+    k_steps = min(args.steps, 200)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(k_steps)]
+    for k in range(k_steps):
+        ly = L[k % layers]
+        rt.set_kernel_events(*kev[k])
+        call(ly)
+    torch.cuda.synchronize()
+    kernel_ms = sum(a.elapsed_time(b) for a, b in kev) / k_steps
+    k_ms = torch.tensor([kernel_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(k_ms, op=dist.ReduceOp.MAX)
+    kernel_ms = float(k_ms.item())
+
     # ---- outputs of every rank gathered once, after timing (the only collective)
     if world > 1:
         gathered = [torch.empty_like(L[0]["out"]) for _ in range(world)]
@@ -384,7 +399,7 @@ def main() -> None:
     errors = rt.device_errors(dev)
     if rank == 0:
         peak, peak_kind = load_peaks()
-        achieved = kvb / (ms_max / 1e3 / args.steps) / 1e9
+        achieved = kvb / (kernel_ms / 1e3) / 1e9   # KV bytes per launch / attention-kernel time
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5),
@@ -401,7 +416,10 @@ def main() -> None:
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": profile_traffic(args.workload),
-                         "per_launch_bytes": kvb, "kernel": "mla_decode_kernel (+ split combine)"},
+                         "per_launch_bytes": kvb, "kernel_ms": round(kernel_ms, 5),
+                         "kernel": ("decode_fp4_dense_kernel" if not wl["topk"] else "mla_decode_kernel<sparse>"),
+                         "step_frac_in_kernel": round(kernel_ms / (ms_max / args.steps), 3),
+                         "splits": splits},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps},
             "gpu_launches": args.steps * launches_per_step,

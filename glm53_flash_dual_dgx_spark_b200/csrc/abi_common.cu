@@ -8,6 +8,7 @@ namespace nvfp4kv {
 
 namespace {
 thread_local std::string g_last_error;
+thread_local cudaEvent_t g_ev_start = nullptr, g_ev_stop = nullptr;
 std::mutex g_sm_mutex;
 int g_sm_count[64] = {0};
 }  // namespace
@@ -41,8 +42,22 @@ int device_sm_count() {
     return g_sm_count[dev];
 }
 
+void take_kernel_events(cudaEvent_t* start, cudaEvent_t* stop) {
+    *start = g_ev_start;
+    *stop = g_ev_stop;
+    g_ev_start = g_ev_stop = nullptr;
+}
+
 }  // namespace nvfp4kv
 
 extern "C" int nvfp4kv_version(void) { return 100; }
+
+extern "C" int nvfp4kv_set_kernel_events(void* start, void* stop) {
+    if ((start == nullptr) != (stop == nullptr))
+        return nvfp4kv::fail(NVFP4KV_EINVAL, "set_kernel_events: give both events or neither");
+    nvfp4kv::g_ev_start = static_cast<cudaEvent_t>(start);
+    nvfp4kv::g_ev_stop = static_cast<cudaEvent_t>(stop);
+    return NVFP4KV_OK;
+}
 
 extern "C" const char* nvfp4kv_last_error(void) { return nvfp4kv::g_last_error.c_str(); }

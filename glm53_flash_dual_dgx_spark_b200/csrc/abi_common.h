@@ -19,4 +19,8 @@ int check_launch(const char* what);
 // Number of SMs of the current device (cached per device).
 int device_sm_count();
 
+// Measurement hook (nvfp4kv_set_kernel_events): events to record around the next main
+// attention kernel launched by the calling thread.  Returns them and clears the hook.
+void take_kernel_events(cudaEvent_t* start, cudaEvent_t* stop);
+
 }  // namespace nvfp4kv

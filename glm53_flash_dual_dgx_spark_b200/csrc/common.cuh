@@ -146,6 +146,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking test of the phase with parity `parity` (never suspends the thread, unlike
+// try_wait): for probing whether optional work is ready.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait on the phase with parity `parity`.  `abort_flag` lives in shared memory:
 // once one thread of the CTA has timed out every later wait of the CTA returns at once,
 // so a broken pipeline ends in about one timeout instead of one per wait.  Inlined so a

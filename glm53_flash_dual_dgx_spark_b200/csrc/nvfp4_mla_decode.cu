@@ -685,6 +685,23 @@ extern "C" int nvfp4kv_mla_decode_workspace_size(int batch, int q_len, int num_h
     return NVFP4KV_OK;
 }
 
+extern "C" int nvfp4kv_mla_decode_plan(int batch, int q_len, int num_heads, int max_seq_len,
+                                       int sparse_topk, int* splits, int* launches) {
+    using namespace nvfp4kv;
+    if (!splits || !launches) return fail(NVFP4KV_EINVAL, "mla_decode_plan: null output");
+    if (batch < 0 || q_len < 1 || num_heads < 1 || max_seq_len < 0 || sparse_topk < 0)
+        return fail(NVFP4KV_EINVAL, "mla_decode_plan: bad shape");
+    if (batch == 0) {
+        *splits = 0;
+        *launches = 0;
+        return NVFP4KV_OK;
+    }
+    const DecodePlan pl = make_decode_plan(batch, q_len, num_heads, max_seq_len, sparse_topk);
+    *splits = pl.splits;
+    *launches = 1 + (pl.splits > 1 ? 1 : 0) + (sparse_topk > 0 ? 0 : 1);   // (Q prep) + attention + (combine)
+    return NVFP4KV_OK;
+}
+
 extern "C" int nvfp4kv_mla_decode(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,
                                   const uint8_t* pool, int64_t pool_rows,
                                   const int32_t* tables, int64_t tables_stride,
@@ -759,8 +776,12 @@ extern "C" int nvfp4kv_mla_decode(const void* q, int64_t q_stride_b, int64_t q_s
     int rc;
     if (sparse_topk > 0) {
         if ((rc = ensure_smem_attr<true>()) != NVFP4KV_OK) return rc;
+        cudaEvent_t ev0, ev1;
+        take_kernel_events(&ev0, &ev1);
+        if (ev0 && cudaEventRecord(ev0, st) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaEventRecord failed");
         mla_decode_kernel<true><<<grid, kThreads, kSmemBytes, st>>>(prm);
         if ((rc = check_launch("nvfp4kv_mla_decode")) != NVFP4KV_OK) return rc;
+        if (ev1 && cudaEventRecord(ev1, st) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaEventRecord failed");
     } else {
         DecodeArgs a{};
         a.q = q; a.q_sb = q_stride_b; a.q_sq = q_stride_q; a.q_sh = q_stride_h;

@@ -855,8 +855,13 @@ int launch_decode_fp4_dense(const DecodeArgs& a, const DecodePlan& pl, cudaStrea
     p.qimg = a.qimg;
     p.err = a.err;
     const dim3 grid(static_cast<unsigned>(a.batch * pl.groups * pl.splits));
+    cudaEvent_t ev0, ev1;
+    take_kernel_events(&ev0, &ev1);
+    if (ev0 && cudaEventRecord(ev0, st) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaEventRecord failed");
     decode_fp4_dense_kernel<<<grid, kThreads, kSmemBytes, st>>>(p, tm_codes, tm_scales);
-    return check_launch("nvfp4kv_mla_decode (fp4 dense)");
+    if ((rc = check_launch("nvfp4kv_mla_decode (fp4 dense)")) != NVFP4KV_OK) return rc;
+    if (ev1 && cudaEventRecord(ev1, st) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaEventRecord failed");
+    return NVFP4KV_OK;
 }
 
 }  // namespace nvfp4kv

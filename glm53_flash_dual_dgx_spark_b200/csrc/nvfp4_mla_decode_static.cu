@@ -1,25 +1,28 @@
-// nvfp4kv_mla_decode_static: the fused NVFP4 MLA decode with its split-K partials kept in a
-// fixed file-scope device array instead of a caller-provided workspace.
+// nvfp4kv_mla_decode_static: the fused NVFP4 MLA decode with its workspace (split-K partials,
+// prepared Q) kept in a fixed file-scope device array instead of a caller-provided one.
 //
 // Some callers cannot allocate device memory on the decode path: a host binding with no
 // caching allocator of its own (a cgo / JNI / ctypes caller) would have to cudaMalloc per
 // call, which synchronises the whole device and can fail with out-of-memory in the middle of
 // a serving step; and an engine that has handed all free HBM to the KV pool after profiling
 // has no headroom left for a per-call workspace.  This entry point needs neither: the
-// partials live in `g_decode_scratch`, which the CUDA module reserves once when it is
-// loaded on a device.
+// workspace (split partials, prepared Q) lives in `g_decode_scratch`, which the CUDA module
+// reserves once when it is loaded on a device.
 //
 // Limits:
-//   - at most kStaticScratchBytes (32 MiB) of partials; nvfp4kv_mla_decode_workspace_size()
+//   - at most kStaticScratchBytes (32 MiB) of workspace; nvfp4kv_mla_decode_workspace_size()
 //     of the shape must not exceed it (larger shapes are rejected with NVFP4KV_EWORKSPACE).
 //     On a 148-SM device the split planner keeps splits * (batch * head groups) <= 148, so
-//     the largest request is 148 * 64 rows * 514 floats = 19.5 MB and every shape fits;
+//     the split partials never pass 148 * 64 rows * 514 floats = 19.5 MB; the dense path adds
+//     72.25 KB of prepared Q per 64-row query group, which stays within the scratch up to
+//     453 groups (e.g. batch 453 at 64 heads and q_len 1);
 //   - one scratch array per device: two calls whose kernels overlap on the same device (on
 //     different streams, or from different host threads) race on it.  Calls must be ordered
 //     on one stream or otherwise serialised;
 //   - nothing in the scratch needs to start at zero: every split CTA writes its (max, sum)
 //     pair for all 64 rows of its unit, and writes its O rows whenever its sum can be
-//     non-zero, before the combine kernel reads them;
+//     non-zero, before the combine kernel reads them; the Q preparation kernel writes every
+//     byte of the prepared-Q images before the attention kernel reads them;
 //   - the first call on each device looks up the array's address (cudaGetSymbolAddress,
 //     with that device current).  Make that first call before any stream capture begins.
 #include <cuda_runtime.h>
@@ -79,7 +82,7 @@ extern "C" int nvfp4kv_mla_decode_static(const void* q, int64_t q_stride_b, int6
     if (rc != NVFP4KV_OK) return rc;
     if (need > kStaticScratchBytes)
         return fail(NVFP4KV_EWORKSPACE,
-                    "mla_decode_static: shape needs %zu bytes of split partials, the static scratch "
+                    "mla_decode_static: shape needs %zu bytes of workspace, the static scratch "
                     "holds %zu; use nvfp4kv_mla_decode with a caller workspace",
                     need, kStaticScratchBytes);
     void* scratch = nullptr;

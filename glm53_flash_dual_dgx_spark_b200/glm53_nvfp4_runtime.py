@@ -230,6 +230,29 @@ def mla_decode_workspace_size(batch: int, q_len: int, num_heads: int, max_seq_le
     return int(out.value)
 
 
+def mla_decode_plan(batch: int, q_len: int, num_heads: int, max_seq_len: int,
+                    sparse_mla_top_k: int = 0, device=None) -> tuple[int, int]:
+    """(token splits per 64-row query group, kernel launches per mla_decode call)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    splits, launches = ctypes.c_int(0), ctypes.c_int(0)
+    with _on_device(dev):
+        rc = _lib.lib().nvfp4kv_mla_decode_plan(batch, q_len, num_heads, max_seq_len, sparse_mla_top_k,
+                                                ctypes.byref(splits), ctypes.byref(launches))
+    _lib.check(rc, "nvfp4kv_mla_decode_plan")
+    return int(splits.value), int(launches.value)
+
+
+def set_kernel_events(start: torch.cuda.Event | None, stop: torch.cuda.Event | None) -> None:
+    """Make the calling thread's next mla_decode record `start` / `stop` immediately around its
+    attention kernel (a measurement hook; both None clears it)."""
+    for e in (start, stop):
+        if e is not None and not e.cuda_event:
+            e.record()   # torch creates the CUDA event on first record; the library re-records it
+    _lib.check(_lib.lib().nvfp4kv_set_kernel_events(
+        ctypes.c_void_p(start.cuda_event) if start is not None else None,
+        ctypes.c_void_p(stop.cuda_event) if stop is not None else None), "nvfp4kv_set_kernel_events")
+
+
 def _workspace(dev: torch.device, nbytes: int, given: torch.Tensor | None) -> torch.Tensor | None:
     if nbytes == 0:
         return None

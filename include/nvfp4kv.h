@@ -134,17 +134,32 @@ int nvfp4kv_mla_decode(const void* q, int64_t q_stride_b, int64_t q_stride_q, in
 int nvfp4kv_mla_decode_workspace_size(int batch, int q_len, int num_heads, int max_seq_len,
                                       int sparse_topk, size_t* bytes);
 
+/* Split plan of nvfp4kv_mla_decode for this shape on the current device: token splits per
+ * 64-row query group, and kernel launches per call (dense: Q preparation + attention +
+ * split combine when splits > 1; sparse: attention + combine when splits > 1).  No
+ * counterpart in the reference; for schedulers and benchmarks. */
+int nvfp4kv_mla_decode_plan(int batch, int q_len, int num_heads, int max_seq_len,
+                            int sparse_topk, int* splits, int* launches);
+
+/* Measurement hook, no counterpart in the reference: the calling thread's next
+ * nvfp4kv_mla_decode (or _static) call records the CUDA events `start` and `stop`
+ * (cudaEvent_t) on its stream immediately before and after its attention kernel, then the
+ * hook clears itself.  Both NULL clears it. */
+int nvfp4kv_set_kernel_events(void* start, void* stop);
+
 /* Capacity of the device scratch array behind nvfp4kv_mla_decode_static. */
 #define NVFP4KV_STATIC_SCRATCH_BYTES 33554432u
 
 /*
- * nvfp4kv_mla_decode without a workspace argument: the split-K partials go to a file-scope
- * device array of NVFP4KV_STATIC_SCRATCH_BYTES (32 MiB, reserved per device when the module
- * loads), so the call allocates nothing.  No counterpart in the reference (its decode takes
- * a workspace buffer); it is for callers that cannot allocate device memory per call.
+ * nvfp4kv_mla_decode without a workspace argument: its workspace (split-K partials, prepared
+ * Q) goes to a file-scope device array of NVFP4KV_STATIC_SCRATCH_BYTES (32 MiB, reserved per
+ * device when the module loads), so the call allocates nothing.  No counterpart in the
+ * reference (its decode takes a workspace buffer); it is for callers that cannot allocate
+ * device memory per call.
  * Same arguments, semantics and errors as nvfp4kv_mla_decode, plus:
  *   - NVFP4KV_EWORKSPACE if nvfp4kv_mla_decode_workspace_size() of the shape exceeds the
- *     scratch (no shape does on a 148-SM device);
+ *     scratch (on a 148-SM device: dense calls with more than 453 query groups of 64 rows,
+ *     e.g. batch > 453 at 64 heads and q_len 1);
  *   - the first call on a device looks up the scratch address with that device current;
  *     make it before any stream capture begins;
  *   - one scratch per device: calls whose kernels overlap on a device race on it.

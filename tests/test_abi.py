@@ -21,7 +21,7 @@ def declared_functions():
 def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     names = declared_functions()
-    assert len(names) == 8, names
+    assert len(names) == 10, names
     for n in names:
         assert hasattr(lib, n), n
     assert set(names) == set(_lib.SIGNATURES)
@@ -86,6 +86,20 @@ def test_workspace_size_formula():
     assert lib.nvfp4kv_mla_decode_workspace_size(16, 1, 64, 0, 2048, ctypes.byref(out)) == _lib.OK
     assert out.value == 8 * 16 * 64 * 514 * 4     # sparse: 8 splits of 2 tiles, no prepared Q
     assert lib.nvfp4kv_mla_decode_workspace_size(-1, 1, 64, 8192, 0, ctypes.byref(out)) == _lib.EINVAL
+
+
+def test_decode_plan():
+    lib = _lib.lib()
+    splits, launches = ctypes.c_int(), ctypes.c_int()
+    assert lib.nvfp4kv_mla_decode_plan(16, 1, 64, 8192, 0, ctypes.byref(splits), ctypes.byref(launches)) == _lib.OK
+    assert (splits.value, launches.value) == (8, 3)        # Q preparation + attention + combine
+    assert lib.nvfp4kv_mla_decode_plan(256, 1, 64, 8192, 0, ctypes.byref(splits), ctypes.byref(launches)) == _lib.OK
+    assert (splits.value, launches.value) == (1, 2)
+    assert lib.nvfp4kv_mla_decode_plan(16, 1, 64, 0, 2048, ctypes.byref(splits), ctypes.byref(launches)) == _lib.OK
+    assert (splits.value, launches.value) == (8, 2)        # sparse: attention + combine
+    assert lib.nvfp4kv_mla_decode_plan(1, 0, 64, 8192, 0, ctypes.byref(splits), ctypes.byref(launches)) == _lib.EINVAL
+    assert lib.nvfp4kv_set_kernel_events(None, None) == _lib.OK
+    assert lib.nvfp4kv_set_kernel_events(ctypes.c_void_p(1), None) == _lib.EINVAL
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
