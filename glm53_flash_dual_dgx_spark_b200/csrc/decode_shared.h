@@ -17,7 +17,7 @@ constexpr int kDecMaxSplits = 64;   // split-K partitions per group
 constexpr size_t kQImageBytes = 65536 + 8192 + 256;
 
 struct DecodePlan {
-    int groups, splits, tokens_per_split;
+    int groups, splits, tiles_total;   // split s: tiles [s T / splits, (s+1) T / splits)
     size_t part_bytes;   // splits * batch * groups * 64 * (512 + 2) floats when splits > 1, else 0
     size_t qimg_bytes;   // batch * groups * kQImageBytes on the dense path, else 0
     size_t ws_bytes;     // part_bytes + qimg_bytes

@@ -90,7 +90,7 @@ struct DecodeParams {
     int sparse, topk;
     int page_shift;
     int64_t num_pages;
-    int max_seq_len, tokens_per_split;
+    int max_seq_len, tiles_total;   // tiles of the planned context, spread over the splits
     float scale_log2, bmm2_scale;
     __nv_bfloat16* out;
     int64_t o_sb, o_sq, o_sh;
@@ -145,8 +145,9 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const DecodePar
         L = cap;
     }
     if (L < 0) L = 0;
-    const int start = s * p.tokens_per_split;
-    const int end = min(start + p.tokens_per_split, L);
+    // split s covers tiles [s T / splits, (s + 1) T / splits) of the planned context
+    const int start = static_cast<int>((static_cast<int64_t>(s) * p.tiles_total) / p.splits) * kTile;
+    const int end = min(static_cast<int>((static_cast<int64_t>(s + 1) * p.tiles_total) / p.splits) * kTile, L);
     const int n_tiles = end > start ? (end - start + kTile - 1) / kTile : 0;
     const int rows_total = p.q_len * p.num_heads;
     const int rows_here = min(kNQ, rows_total - g * kNQ);
@@ -661,10 +662,8 @@ DecodePlan make_decode_plan(int batch, int q_len, int num_heads, int max_seq_len
     int want = units >= sms ? 1 : sms / units;
     want = want < 1 ? 1 : (want > kMaxSplits ? kMaxSplits : want);
     want = want > tiles ? tiles : want;
-    const int tiles_per_split = (tiles + want - 1) / want;
-    pl.tokens_per_split = tiles_per_split * kTile;
-    pl.splits = (tiles + tiles_per_split - 1) / tiles_per_split;
-    if (pl.splits < 1) pl.splits = 1;
+    pl.tiles_total = tiles;
+    pl.splits = want < 1 ? 1 : want;   // split sizes differ by at most one tile
     pl.part_bytes = pl.splits > 1
                         ? static_cast<size_t>(pl.splits) * units * kNQ * (kLatent + 2) * sizeof(float)
                         : 0;
@@ -761,7 +760,7 @@ extern "C" int nvfp4kv_mla_decode(const void* q, int64_t q_stride_b, int64_t q_s
     prm.page_shift = page_shift;
     prm.num_pages = sparse_topk > 0 ? 0 : pool_rows / page_size;
     prm.max_seq_len = sparse_topk > 0 ? sparse_topk : max_seq_len;
-    prm.tokens_per_split = pl.tokens_per_split;
+    prm.tiles_total = pl.tiles_total;
     prm.scale_log2 = bmm1_scale * 1.4426950408889634f;
     prm.bmm2_scale = bmm2_scale;
     prm.out = static_cast<__nv_bfloat16*>(out);

@@ -108,7 +108,7 @@ struct Fp4Params {
     int batch, q_len, num_heads, groups, splits;
     int page_shift, box_rows;
     int64_t num_pages;
-    int max_seq_len, tokens_per_split;
+    int max_seq_len, tiles_total;   // tiles of the planned context, spread over the splits
     float bmm2_scale;
     __nv_bfloat16* out;
     int64_t o_sb, o_sq, o_sh;
@@ -339,8 +339,9 @@ decode_fp4_dense_kernel(const __grid_constant__ Fp4Params p, const __grid_consta
         L = p.max_seq_len;
     }
     if (L < 0) L = 0;
-    const int start = s * p.tokens_per_split;
-    const int end = min(start + p.tokens_per_split, L);
+    // split s covers tiles [s T / splits, (s + 1) T / splits) of the planned context
+    const int start = static_cast<int>((static_cast<int64_t>(s) * p.tiles_total) / p.splits) * kTile;
+    const int end = min(static_cast<int>((static_cast<int64_t>(s + 1) * p.tiles_total) / p.splits) * kTile, L);
     const int n_tiles = end > start ? (end - start + kTile - 1) / kTile : 0;
     const int rows_here = min(kNQ, p.q_len * p.num_heads - g * kNQ);
 
@@ -847,7 +848,7 @@ int launch_decode_fp4_dense(const DecodeArgs& a, const DecodePlan& pl, cudaStrea
     p.page_shift = a.page_shift; p.box_rows = box_rows;
     p.num_pages = a.pool_rows / a.page_size;
     p.max_seq_len = a.max_seq_len;
-    p.tokens_per_split = pl.tokens_per_split;
+    p.tiles_total = pl.tiles_total;
     p.bmm2_scale = a.bmm2_scale;
     p.out = static_cast<__nv_bfloat16*>(a.out);
     p.o_sb = a.o_sb; p.o_sq = a.o_sq; p.o_sh = a.o_sh;
