@@ -417,7 +417,7 @@ def main() -> None:
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": profile_traffic(args.workload),
                          "per_launch_bytes": kvb, "kernel_ms": round(kernel_ms, 5),
-                         "kernel": ("decode_fp4_dense_kernel" if not wl["topk"] else "mla_decode_kernel<sparse>"),
+                         "kernel": "decode_fp4_kernel<sparse>" if wl["topk"] else "decode_fp4_kernel<dense>",
                          "step_frac_in_kernel": round(kernel_ms / (ms_max / args.steps), 3),
                          "splits": splits},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,

@@ -12,14 +12,14 @@ constexpr int kDecTile = 128;       // tokens per tile
 constexpr int kDecRows = 64;        // query rows per CTA (one "group")
 constexpr int kDecMaxSplits = 64;   // split-K partitions per group
 
-// Bytes of one query group's prepared Q (dense path): the four NVFP4 terms as the fused
+// Bytes of one query group's prepared Q: the four NVFP4 terms as the fused
 // kernel's shared-memory image (64 KB), their scales (8 KB) and 64 per-row score factors.
 constexpr size_t kQImageBytes = 65536 + 8192 + 256;
 
 struct DecodePlan {
     int groups, splits, tiles_total;   // split s: tiles [s T / splits, (s+1) T / splits)
     size_t part_bytes;   // splits * batch * groups * 64 * (512 + 2) floats when splits > 1, else 0
-    size_t qimg_bytes;   // batch * groups * kQImageBytes on the dense path, else 0
+    size_t qimg_bytes;   // batch * groups * kQImageBytes
     size_t ws_bytes;     // part_bytes + qimg_bytes
 };
 DecodePlan make_decode_plan(int batch, int q_len, int num_heads, int max_seq_len, int sparse_topk);
@@ -40,11 +40,12 @@ struct DecodeArgs {
     int64_t o_sb, o_sq, o_sh;
     float* part_o;    // [splits][batch][groups][64][512] when splits > 1
     float* part_ml;   // [splits][batch][groups][64][2]
-    uint8_t* qimg;    // [batch][groups][kQImageBytes] (dense path)
+    uint8_t* qimg;    // [batch][groups][kQImageBytes]
     int32_t* err;
 };
 
-// Dense (paged) decode with the QK^T product on the block-scaled fp4 tensor-core path.
-int launch_decode_fp4_dense(const DecodeArgs& a, const DecodePlan& pl, cudaStream_t st);
+// Q preparation + the fused decode kernel (QK^T on the block-scaled fp4 tensor-core path),
+// paged (sparse_topk == 0) or top-k rows (sparse_topk > 0).
+int launch_decode_fp4(const DecodeArgs& a, const DecodePlan& pl, cudaStream_t st);
 
 }  // namespace nvfp4kv

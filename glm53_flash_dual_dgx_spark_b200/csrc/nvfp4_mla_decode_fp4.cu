@@ -15,10 +15,14 @@
 //   O^T[d, n] += V^T[d, t] P^T[t, n]      M = 128 dims (4 blocks), N = 64 query rows, K = 16.
 //
 // Work unit (one CTA): query group (b, g) of up to 64 rows (MTP token i, head h) x token split.
-// Warps: 0-3 softmax (thread = token of the tile = TMEM lane), 4 MMA issue, 5-8 producers
-// (lane 0 of warp 5 also issues the TMA loads).  Per 128-token tile i:
-//   TMA      3-slot ring of raw tiles: codes [2 x 128 rows x 128 B] swizzled + scales [128 x 32 B];
-//            pages missing or beyond the context load as out-of-range boxes (zeros).
+// Warps: 0-7 softmax (warp w: TMEM sub-partition w & 3 = tokens of the tile, query rows
+// 32 (w >> 2) .. +32), 8 MMA issue, 9-12 producers, 13 loads.  Per 128-token tile i:
+//   loads    ring of tiles: codes [2 x 128 rows x 128 B] swizzled + scales [128 x 32 B].
+//            Dense (paged): 3 slots filled by TMA boxes straight from the pages; pages missing
+//            or beyond the context load as out-of-range boxes (zeros).  Sparse (top-k rows):
+//            2 slots; the warp bulk-copies the 128 rows (288 B each) into a staging buffer in
+//            the third slot's space and rearranges them into the ring layout, zeros for
+//            masked rows, so everything downstream is shared with the dense path.
 //   producers  V chunks of 16 tokens -> fp16 [8 d-atoms x 16 tokens x 128 B] (2 buffers).
 //   MMA      QK(i): 16 fp4 MMAs M128 N128 K64 -> S^T; PV(i-1): 8 chunks x 4 fp16 MMAs.
 //   softmax  S^T row t -> x = s * log2(e) * bmm1_scale, masked; the running max of each query
@@ -44,7 +48,7 @@ constexpr int kTile = kDecTile;                   // 128 tokens: QK M
 constexpr int kNQ = kDecRows;                     // 64 query rows: PV N
 constexpr int kChunk = 16;                        // tokens per V chunk = PV K
 constexpr int kChunks = kTile / kChunk;           // 8
-constexpr int kSlots = 3;                         // raw-tile ring depth
+constexpr int kSlots = 3;                         // tile ring depth (dense; sparse uses 2 + staging)
 constexpr int kVBufs = 2;                         // V chunk buffers
 constexpr int kSoftmaxWarps = 8;                  // 2 per TMEM sub-partition, 32 query rows each
 constexpr int kMmaWarp = 8;
@@ -84,6 +88,7 @@ enum {
     B_V_FULL,                      // [kVBufs] V chunk written
     B_V_EMPTY = B_V_FULL + kVBufs, // [kVBufs] PV finished reading the V chunk
     B_Q = B_V_EMPTY + kVBufs,      // prepared Q landed (set-up)
+    B_STAGE,                       // sparse: rows of the next tile landed in the staging buffer
     kNumBars
 };
 constexpr int SM_IDX = SM_BARS + ((kNumBars * 8 + 15) / 16) * 16;
@@ -102,6 +107,8 @@ constexpr uint32_t kTSFA = 384;  // 2 slots x 32 columns: pool scales of a tile
 constexpr uint32_t kTSFB = 448;  // 2 passes x 32 columns: Q-term scales
 
 struct Fp4Params {
+    const uint8_t* pool;           // sparse: rows are bulk-copied from here
+    int64_t pool_rows;
     const int32_t* tables;
     int64_t tables_stride;
     const int32_t* seq_lens;
@@ -226,6 +233,73 @@ __device__ __forceinline__ void load_tile(const Fp4Params& p, const void* tm_cod
     }
 }
 
+// Pool row of token position `pos` (< end), or -1 when the token is masked.  Dense: the page
+// table entry must name a page of the pool.  Sparse: the table holds pool rows, -1 padded;
+// with `report`, entries < -1 or >= pool_rows set NVFP4KV_DEVERR_BAD_INDEX.
+template <bool kSparse>
+__device__ __forceinline__ int64_t token_row(const Fp4Params& p, const int* sidx, bool staged, int idx_base,
+                                             int b, int pos, bool report) {
+    if constexpr (kSparse) {
+        const int idx = staged ? sidx[pos - idx_base] : __ldg(p.tables + b * p.tables_stride + pos);
+        if (idx < 0 || idx >= p.pool_rows) {
+            if (report && idx != -1) set_error(p.err, NVFP4KV_DEVERR_BAD_INDEX);
+            return -1;
+        }
+        return idx;
+    } else {
+        const int pg = page_id(p, sidx, staged, idx_base, b, pos);
+        if (pg < 0 || pg >= p.num_pages) return -1;
+        return (static_cast<int64_t>(pg) << p.page_shift) | (pos & ((1 << p.page_shift) - 1));
+    }
+}
+
+// Sparse: bulk-copy the rows of tile `tile_start` (288 B each, lane l copies rows l + 32k)
+// into the staging buffer at `stage`, row r at r * 288.  Masked rows are not copied; the
+// transaction count covers exactly the rows that are.  Returns bit k set when row l + 32k was.
+__device__ __forceinline__ uint32_t load_rows(const Fp4Params& p, uint32_t stage, uint32_t bar_stage,
+                                              const int* sidx, bool staged, int idx_base, int b,
+                                              int tile_start, int end, int lane) {
+    int64_t rows[4];
+    uint32_t live = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int pos = tile_start + 32 * k + lane;
+        rows[k] = pos < end ? token_row<true>(p, sidx, staged, idx_base, b, pos, true) : -1;
+        live |= static_cast<uint32_t>(rows[k] >= 0) << k;
+    }
+    int n = __popc(live);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) n += __shfl_xor_sync(0xFFFFFFFFu, n, off);
+    if (lane == 0) mbar_arrive_expect_tx(bar_stage, static_cast<uint32_t>(n) * kRowBytes);
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        if (rows[k] >= 0)
+            bulk_copy_g2s(stage + (32 * k + lane) * kRowBytes, p.pool + rows[k] * kRowBytes, kRowBytes,
+                          bar_stage);
+    return live;
+}
+
+// Sparse: staged rows -> ring slot layout (codes in 128-byte swizzled K-major atoms, scales
+// at 32 B per row); rows whose bit in `live` is clear become zeros.  Lane l moves rows l + 32k.
+__device__ __forceinline__ void rows_to_slot(const uint8_t* stage, uint8_t* slot, uint32_t live, int lane) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int r = 32 * k + lane;
+        const bool ok = (live >> k) & 1u;
+        const uint4* src = reinterpret_cast<const uint4*>(stage + r * kRowBytes);
+        uint8_t* dst = slot + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+            const uint4 v = ok ? src[c] : make_uint4(0u, 0u, 0u, 0u);
+            *reinterpret_cast<uint4*>(dst + (c >> 3) * 16384 + (((c & 7) ^ (r & 7)) << 4)) = v;
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            reinterpret_cast<uint4*>(slot + kCodeBytes + r * 32)[h] = ok ? src[16 + h] : make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
 // Pool scales of the tile in `slot` -> TMEM scale-factor columns `col` of this warp's
 // sub-partition: column 4kk+q of lane r holds the 4 scales (dims 64kk..64kk+63) of token
 // 32q + r.  Every sub-partition needs a full copy.
@@ -319,9 +393,15 @@ __device__ __forceinline__ void probs32(const float (&sraw)[32], const float* qs
     }
 }
 
+// kSparse: the table holds pool rows (top-k, -1 padded) instead of page ids; the tensor maps
+// are unused.
+template <bool kSparse>
 __global__ void __launch_bounds__(kThreads, 1)
-decode_fp4_dense_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ CUtensorMap tm_codes,
-                        const __grid_constant__ CUtensorMap tm_scales) {
+decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ CUtensorMap tm_codes,
+                  const __grid_constant__ CUtensorMap tm_scales) {
+    constexpr int kRing = kSparse ? 2 : kSlots;
+    constexpr int SM_STAGING = SM_STAGE + 2 * kSlotBytes;   // sparse: 128 raw rows of 288 B
+    static_assert(kTile * kRowBytes <= kSlotBytes, "staging buffer fits a ring slot");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -373,6 +453,7 @@ decode_fp4_dense_kernel(const __grid_constant__ Fp4Params p, const __grid_consta
         mbar_init(bar(B_P_FULL), kSoftmaxWarps);
         mbar_init(bar(B_PV_DONE), 1);
         mbar_init(bar(B_Q), 1);
+        mbar_init(bar(B_STAGE), 1);
         flags[1] = 0;
         mbar_fence_init();
     }
@@ -380,9 +461,9 @@ decode_fp4_dense_kernel(const __grid_constant__ Fp4Params p, const __grid_consta
         tmem_alloc(sbase + SM_FLAGS, kTmemCols);
         tmem_relinquish();
     }
-    // page ids of this split
-    const int idx_base = start >> p.page_shift;
-    const int idx_count = end > start ? ((end - 1) >> p.page_shift) - idx_base + 1 : 0;
+    // page ids (dense) / pool rows (sparse) of this split
+    const int idx_base = kSparse ? start : start >> p.page_shift;
+    const int idx_count = end <= start ? 0 : kSparse ? end - start : ((end - 1) >> p.page_shift) - idx_base + 1;
     const bool staged = idx_count <= kMaxIdx;
     if (staged)
         for (int k = threadIdx.x; k < idx_count; k += kThreads)
@@ -400,8 +481,34 @@ decode_fp4_dense_kernel(const __grid_constant__ Fp4Params p, const __grid_consta
             bulk_copy_g2s(sbase + SM_QB, img, 2 * kCodeBytes, bar(B_Q));
             bulk_copy_g2s(sbase + SM_PT, img + 2 * kCodeBytes, 2 * 4096, bar(B_Q));
             bulk_copy_g2s(sbase + SM_QS, img + 2 * kCodeBytes + 2 * 4096, 256, bar(B_Q));
-            tma_prefetch_desc(&tm_codes);
-            tma_prefetch_desc(&tm_scales);
+            if constexpr (!kSparse) {
+                tma_prefetch_desc(&tm_codes);
+                tma_prefetch_desc(&tm_scales);
+            }
+        }
+        if constexpr (kSparse) {
+            // tile j: rows -> staging -> slot j & 1 once QK(j-2) and the producers are done with it
+            uint32_t live = 0;
+            if (n_tiles > 0)
+                live = load_rows(p, sbase + SM_STAGING, bar(B_STAGE), sidx, staged, idx_base, b, start, end, lane);
+#pragma unroll 1
+            for (int j = 0; j < n_tiles; ++j) {
+                const int slot = j & 1;
+                mbar_wait(bar(B_STAGE), j & 1, abort_flag, p.err);
+                if (j >= 2) {
+                    mbar_wait(bar(B_FREE + slot), ((j - 2) >> 1) & 1, abort_flag, p.err);
+                    mbar_wait(bar(B_QKD + slot), ((j - 2) >> 1) & 1, abort_flag, p.err);
+                }
+                rows_to_slot(smem + SM_STAGING, smem + SM_STAGE + slot * kSlotBytes, live, lane);
+                // the slot is read by the tensor core; the staging buffer is refilled by bulk copies
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(B_FULL + slot));
+                if (j + 1 < n_tiles)
+                    live = load_rows(p, sbase + SM_STAGING, bar(B_STAGE), sidx, staged, idx_base, b,
+                                     start + (j + 1) * kTile, end, lane);
+            }
+        } else if (lane == 0) {
             for (int j = 0; j < kSlots && j < n_tiles; ++j)
                 load_tile(p, &tm_codes, &tm_scales, sbase, bar(B_FULL + j), sidx, staged, idx_base, b,
                           start + j * kTile, end, j);
@@ -427,8 +534,8 @@ decode_fp4_dense_kernel(const __grid_constant__ Fp4Params p, const __grid_consta
 #pragma unroll 1
         for (int i = 0; i <= n_tiles; ++i) {
             if (i < n_tiles) {
-                const int slot = i % kSlots, fb = i & 1;
-                mbar_wait(bar(B_FULL + slot), (i / kSlots) & 1, abort_flag, p.err);
+                const int slot = i % kRing, fb = i & 1;
+                mbar_wait(bar(B_FULL + slot), (i / kRing) & 1, abort_flag, p.err);
                 mbar_wait(bar(B_SFA_FULL + fb), (i >> 1) & 1, abort_flag, p.err);
                 if (i > 0) mbar_wait(bar(B_S_FREE), (i - 1) & 1, abort_flag, p.err);
                 tc_fence_after();
@@ -477,8 +584,8 @@ decode_fp4_dense_kernel(const __grid_constant__ Fp4Params p, const __grid_consta
         const int pw = warp - kMmaWarp - 1;
 #pragma unroll 1
         for (int i = 0; i < n_tiles; ++i) {
-            const int slot = i % kSlots;
-            mbar_wait(bar(B_FULL + slot), (i / kSlots) & 1, abort_flag, p.err);
+            const int slot = i % kRing;
+            mbar_wait(bar(B_FULL + slot), (i / kRing) & 1, abort_flag, p.err);
             const uint8_t* codes = smem + SM_STAGE + slot * kSlotBytes;
             const uint8_t* scales = codes + kCodeBytes;
 #pragma unroll 1
@@ -581,8 +688,8 @@ decode_fp4_dense_kernel(const __grid_constant__ Fp4Params p, const __grid_consta
             // pool scales of tile i+1 -> its TMEM slot (QK(i-1), the slot's last reader, is
             // complete: S_FULL(i) tracks every earlier MMA)
             if (hh == 0 && i + 1 < n_tiles) {
-                const int slot1 = (i + 1) % kSlots;
-                mbar_wait(bar(B_FULL + slot1), ((i + 1) / kSlots) & 1, abort_flag, p.err);
+                const int slot1 = (i + 1) % kRing;
+                mbar_wait(bar(B_FULL + slot1), ((i + 1) / kRing) & 1, abort_flag, p.err);
                 scales_to_tmem(smem + SM_STAGE + slot1 * kSlotBytes + kCodeBytes,
                                tmem + kTSFA + 32 * ((i + 1) & 1) + lane_base, lane);
                 tc_fence_before();
@@ -603,11 +710,7 @@ decode_fp4_dense_kernel(const __grid_constant__ Fp4Params p, const __grid_consta
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(B_S_FREE));
             const int pos = start + i * kTile + t;
-            bool tok_ok = pos < end;
-            if (tok_ok) {
-                const int pg = page_id(p, sidx, staged, idx_base, b, pos);
-                tok_ok = pg >= 0 && pg < p.num_pages;
-            }
+            const bool tok_ok = pos < end && token_row<kSparse>(p, sidx, staged, idx_base, b, pos, false) >= 0;
             // does any visible score exceed its row's running max by more than 2^8?
             bool grow = false;
 #pragma unroll
@@ -802,12 +905,13 @@ int make_pool_map(CUtensorMap* m, const uint8_t* pool, int64_t pool_rows, uint32
     return NVFP4KV_OK;
 }
 
+template <bool kSparse>
 int ensure_fp4_smem_attr() {
     static int done[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaGetDevice failed");
     if (dev >= 0 && dev < 64 && done[dev]) return NVFP4KV_OK;
-    const cudaError_t e = cudaFuncSetAttribute(decode_fp4_dense_kernel,
+    const cudaError_t e = cudaFuncSetAttribute(decode_fp4_kernel<kSparse>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess)
         return fail(NVFP4KV_ECUDA, "cudaFuncSetAttribute(max dynamic smem %d): %s", kSmemBytes, cudaGetErrorString(e));
@@ -817,21 +921,24 @@ int ensure_fp4_smem_attr() {
 
 }  // namespace
 
-int launch_decode_fp4_dense(const DecodeArgs& a, const DecodePlan& pl, cudaStream_t st) {
-    if (a.page_size < 16)
+int launch_decode_fp4(const DecodeArgs& a, const DecodePlan& pl, cudaStream_t st) {
+    const bool sparse = a.sparse_topk > 0;
+    if (!sparse && a.page_size < 16)
         return fail(NVFP4KV_EINVAL, "mla_decode: page_size must be >= 16 (got %d)", a.page_size);
     if (!a.qimg || reinterpret_cast<uintptr_t>(a.qimg) % 16)
         return fail(NVFP4KV_EWORKSPACE, "mla_decode: no 16-byte aligned workspace for the prepared Q");
     if (a.pool_rows > 0x7FFFFFFFll)
         return fail(NVFP4KV_EINVAL, "mla_decode: pool_rows %lld beyond 2^31 - 1", static_cast<long long>(a.pool_rows));
-    const int box_rows = a.page_size < kTile ? a.page_size : kTile;
-    CUtensorMap tm_codes, tm_scales;
+    const int box_rows = sparse ? 0 : (a.page_size < kTile ? a.page_size : kTile);
+    CUtensorMap tm_codes{}, tm_scales{};
     int rc;
-    if ((rc = make_pool_map(&tm_codes, a.pool, a.pool_rows, 128, box_rows, CU_TENSOR_MAP_SWIZZLE_128B)) != NVFP4KV_OK)
-        return rc;
-    if ((rc = make_pool_map(&tm_scales, a.pool, a.pool_rows, 32, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE)) != NVFP4KV_OK)
-        return rc;
-    if ((rc = ensure_fp4_smem_attr()) != NVFP4KV_OK) return rc;
+    if (!sparse) {
+        if ((rc = make_pool_map(&tm_codes, a.pool, a.pool_rows, 128, box_rows, CU_TENSOR_MAP_SWIZZLE_128B)) != NVFP4KV_OK)
+            return rc;
+        if ((rc = make_pool_map(&tm_scales, a.pool, a.pool_rows, 32, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE)) != NVFP4KV_OK)
+            return rc;
+    }
+    if ((rc = sparse ? ensure_fp4_smem_attr<true>() : ensure_fp4_smem_attr<false>()) != NVFP4KV_OK) return rc;
     QPrepParams qp{};
     qp.q = static_cast<const __nv_bfloat16*>(a.q);
     qp.q_sb = a.q_sb; qp.q_sq = a.q_sq; qp.q_sh = a.q_sh;
@@ -841,13 +948,14 @@ int launch_decode_fp4_dense(const DecodeArgs& a, const DecodePlan& pl, cudaStrea
     q_prep_kernel<<<a.batch * pl.groups * 8, 256, 0, st>>>(qp);
     if ((rc = check_launch("nvfp4kv_mla_decode (Q preparation)")) != NVFP4KV_OK) return rc;
     Fp4Params p{};
+    p.pool = a.pool; p.pool_rows = a.pool_rows;
     p.tables = a.tables; p.tables_stride = a.tables_stride;
     p.seq_lens = a.seq_lens;
     p.batch = a.batch; p.q_len = a.q_len; p.num_heads = a.num_heads;
     p.groups = pl.groups; p.splits = pl.splits;
-    p.page_shift = a.page_shift; p.box_rows = box_rows;
-    p.num_pages = a.pool_rows / a.page_size;
-    p.max_seq_len = a.max_seq_len;
+    p.page_shift = sparse ? 0 : a.page_shift; p.box_rows = box_rows;
+    p.num_pages = sparse ? 0 : a.pool_rows / a.page_size;
+    p.max_seq_len = sparse ? a.sparse_topk : a.max_seq_len;   // seq_lens beyond it are clamped
     p.tiles_total = pl.tiles_total;
     p.bmm2_scale = a.bmm2_scale;
     p.out = static_cast<__nv_bfloat16*>(a.out);
@@ -859,8 +967,12 @@ int launch_decode_fp4_dense(const DecodeArgs& a, const DecodePlan& pl, cudaStrea
     cudaEvent_t ev0, ev1;
     take_kernel_events(&ev0, &ev1);
     if (ev0 && cudaEventRecord(ev0, st) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaEventRecord failed");
-    decode_fp4_dense_kernel<<<grid, kThreads, kSmemBytes, st>>>(p, tm_codes, tm_scales);
-    if ((rc = check_launch("nvfp4kv_mla_decode (fp4 dense)")) != NVFP4KV_OK) return rc;
+    if (sparse)
+        decode_fp4_kernel<true><<<grid, kThreads, kSmemBytes, st>>>(p, tm_codes, tm_scales);
+    else
+        decode_fp4_kernel<false><<<grid, kThreads, kSmemBytes, st>>>(p, tm_codes, tm_scales);
+    if ((rc = check_launch(sparse ? "nvfp4kv_mla_decode (fp4 sparse)" : "nvfp4kv_mla_decode (fp4 dense)")) != NVFP4KV_OK)
+        return rc;
     if (ev1 && cudaEventRecord(ev1, st) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaEventRecord failed");
     return NVFP4KV_OK;
 }

@@ -13,9 +13,9 @@
 //   - at most kStaticScratchBytes (32 MiB) of workspace; nvfp4kv_mla_decode_workspace_size()
 //     of the shape must not exceed it (larger shapes are rejected with NVFP4KV_EWORKSPACE).
 //     On a 148-SM device the split planner keeps splits * (batch * head groups) <= 148, so
-//     the split partials never pass 148 * 64 rows * 514 floats = 19.5 MB; the dense path adds
-//     72.25 KB of prepared Q per 64-row query group, which stays within the scratch up to
-//     453 groups (e.g. batch 453 at 64 heads and q_len 1);
+//     the split partials never pass 148 * 64 rows * 514 floats = 19.5 MB; the prepared Q adds
+//     72.25 KB per 64-row query group, which stays within the scratch up to 453 groups
+//     (e.g. batch 453 at 64 heads and q_len 1);
 //   - one scratch array per device: two calls whose kernels overlap on the same device (on
 //     different streams, or from different host threads) race on it.  Calls must be ordered
 //     on one stream or otherwise serialised;

@@ -135,9 +135,8 @@ int nvfp4kv_mla_decode_workspace_size(int batch, int q_len, int num_heads, int m
                                       int sparse_topk, size_t* bytes);
 
 /* Split plan of nvfp4kv_mla_decode for this shape on the current device: token splits per
- * 64-row query group, and kernel launches per call (dense: Q preparation + attention +
- * split combine when splits > 1; sparse: attention + combine when splits > 1).  No
- * counterpart in the reference; for schedulers and benchmarks. */
+ * 64-row query group, and kernel launches per call (Q preparation + attention, + split
+ * combine when splits > 1).  No counterpart in the reference; for schedulers and benchmarks. */
 int nvfp4kv_mla_decode_plan(int batch, int q_len, int num_heads, int max_seq_len,
                             int sparse_topk, int* splits, int* launches);
 
@@ -158,7 +157,7 @@ int nvfp4kv_set_kernel_events(void* start, void* stop);
  * device memory per call.
  * Same arguments, semantics and errors as nvfp4kv_mla_decode, plus:
  *   - NVFP4KV_EWORKSPACE if nvfp4kv_mla_decode_workspace_size() of the shape exceeds the
- *     scratch (on a 148-SM device: dense calls with more than 453 query groups of 64 rows,
+ *     scratch (on a 148-SM device: calls with more than 453 query groups of 64 rows,
  *     e.g. batch > 453 at 64 heads and q_len 1);
  *   - the first call on a device looks up the scratch address with that device current;
  *     make it before any stream capture begins;

@@ -162,6 +162,41 @@ def test_sparse_topk(rt, topk, pad):
     assert rt.device_errors() == 0
 
 
+def run_sparse(rt, B, H, topk, seq_lens, seed=5, qscale=1.0, pool_pages=256, bad=0.0, pad=0.0):
+    pool_t, pool = make_pool(pool_pages, seed=seed)
+    R = pool_pages * 64
+    g = torch.Generator().manual_seed(seed + 1)
+    # rows drawn with replacement: repeated rows are legal top-k entries
+    idx = torch.randint(0, R, (B, topk), generator=g, dtype=torch.int32)
+    idx[torch.rand(B, topk, generator=g) < pad] = -1
+    nbad = torch.rand(B, topk, generator=g) < bad
+    idx[nbad] = torch.where(torch.rand(B, topk, generator=g) < 0.5, R + 17, -5).to(torch.int32)[nbad]
+    sl = torch.tensor(seq_lens, dtype=torch.int32)
+    q = (torch.randn(B, 1, H, 576, generator=g) * qscale).to(torch.bfloat16)
+    out = rt.mla_decode(q.cuda(), pool_t, None, 128, 512, 64, idx.view(B, 1, topk).cuda(), sl.cuda(), topk,
+                        sparse_mla_top_k=topk, bmm1_scale=SM)
+    ref = O.mla_decode(q.float(), pool, idx.view(B, 1, topk).numpy(), sl.numpy(), sparse=True, bmm1_scale=SM)
+    return out, ref
+
+
+def test_sparse_many_tiles_per_split(rt):
+    """20 entries x 128 heads = 40 query groups: 3 splits of ~11 tiles each, so the 2-slot
+    tile ring wraps many times; ragged counts end tiles mid-way."""
+    out, ref = run_sparse(rt, 20, 128, 4096, [4096, 4000, 3001, 129] * 5)
+    check(out, ref, "sparse many tiles")
+
+
+def test_sparse_peaked_scores(rt):
+    out, ref = run_sparse(rt, 8, 64, 2048, [2048] * 4 + [1500] * 4, qscale=8.0, seed=11)
+    check(out, ref, "sparse peaked")
+
+
+def test_sparse_out_of_range_indices_masked(rt):
+    """Entries < -1 or >= pool_rows are masked like -1 padding and flag BAD_INDEX."""
+    out, ref = run_sparse(rt, 6, 64, 1024, [1024, 1000, 700, 1024, 5, 1024], bad=0.05, pad=0.05, seed=21)
+    check(out, ref, "sparse bad indices", errors_ok=4)
+
+
 def test_sparse_config3_shape(rt):
     """Config 3 at full size: batch 16, 64 heads, 128K context per sequence (pool of
     2,097,152 rows on shuffled pages), top-2048 drawn without replacement (seed 1)."""
