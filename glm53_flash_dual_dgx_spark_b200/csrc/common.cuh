@@ -183,6 +183,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
+// Wait for a phase whatever the abort flag says, still bounded: run before a CTA exits so that
+// no bulk copy or tensor-core operation it issued is still writing its shared or tensor
+// memory, on the abort path too.
+__device__ __forceinline__ void mbar_drain_wait(uint32_t bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer_ns() - t0 > NVFP4KV_WAIT_TIMEOUT_NS) return;
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -113,7 +113,28 @@ DecodePlan make_decode_plan(int batch, int q_len, int num_heads, int max_seq_len
     return pl;
 }
 
+namespace {
+
+// One thread waits on an mbarrier whose single expected arrival never comes.
+__global__ void bounded_wait_selftest_kernel(int32_t* err) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    const uint32_t b = smem_u32(&bar);
+    mbar_init(b, 1);
+    abort_flag = 0;
+    mbar_fence_init();
+    mbar_wait(b, 0, &abort_flag, err);   // returns false after NVFP4KV_WAIT_TIMEOUT_NS
+}
+
+}  // namespace
 }  // namespace nvfp4kv
+
+extern "C" int nvfp4kv_selftest_bounded_wait(int32_t* err_flag, nvfp4kv_stream_t stream) {
+    using namespace nvfp4kv;
+    if (!err_flag) return fail(NVFP4KV_EINVAL, "selftest_bounded_wait: null error word");
+    bounded_wait_selftest_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(err_flag);
+    return check_launch("nvfp4kv_selftest_bounded_wait");
+}
 
 extern "C" int nvfp4kv_mla_decode_workspace_size(int batch, int q_len, int num_heads,
                                                  int max_seq_len, int sparse_topk, size_t* bytes) {

@@ -89,6 +89,7 @@ enum {
     B_V_EMPTY = B_V_FULL + kVBufs, // [kVBufs] PV finished reading the V chunk
     B_Q = B_V_EMPTY + kVBufs,      // prepared Q landed (set-up)
     B_STAGE,                       // sparse: rows of the next tile landed in the staging buffer
+    B_DRAIN,                       // every MMA of the CTA complete (before TMEM is freed)
     kNumBars
 };
 constexpr int SM_IDX = SM_BARS + ((kNumBars * 8 + 15) / 16) * 16;
@@ -454,6 +455,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
         mbar_init(bar(B_PV_DONE), 1);
         mbar_init(bar(B_Q), 1);
         mbar_init(bar(B_STAGE), 1);
+        mbar_init(bar(B_DRAIN), 1);
         flags[1] = 0;
         mbar_fence_init();
     }
@@ -476,6 +478,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
     if (warp == kTmaWarp) {
         // ============================================================ TMA / bulk loads
         if (lane == 0) {
+            // (a kernel-boundary dependency: the Q preparation kernel ran before this launch)
             const uint8_t* img = p.qimg + static_cast<size_t>(b * p.groups + g) * kQImageBytes;
             mbar_arrive_expect_tx(bar(B_Q), static_cast<uint32_t>(kQImageBytes));
             bulk_copy_g2s(sbase + SM_QB, img, 2 * kCodeBytes, bar(B_Q));
@@ -489,40 +492,60 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
         if constexpr (kSparse) {
             // tile j: rows -> staging -> slot j & 1 once QK(j-2) and the producers are done with it
             uint32_t live = 0;
-            if (n_tiles > 0)
+            int issued = 0;   // staging loads issued; load k completes phase k of B_STAGE
+            if (n_tiles > 0) {
                 live = load_rows(p, sbase + SM_STAGING, bar(B_STAGE), sidx, staged, idx_base, b, start, end, lane);
+                issued = 1;
+            }
 #pragma unroll 1
             for (int j = 0; j < n_tiles; ++j) {
                 const int slot = j & 1;
-                mbar_wait(bar(B_STAGE), j & 1, abort_flag, p.err);
+                bool ok = mbar_wait(bar(B_STAGE), j & 1, abort_flag, p.err);
                 if (j >= 2) {
-                    mbar_wait(bar(B_FREE + slot), ((j - 2) >> 1) & 1, abort_flag, p.err);
-                    mbar_wait(bar(B_QKD + slot), ((j - 2) >> 1) & 1, abort_flag, p.err);
+                    ok &= mbar_wait(bar(B_FREE + slot), ((j - 2) >> 1) & 1, abort_flag, p.err);
+                    ok &= mbar_wait(bar(B_QKD + slot), ((j - 2) >> 1) & 1, abort_flag, p.err);
                 }
+                // after an abort nothing more is issued (the drain below waits for what was)
+                if (!__all_sync(0xFFFFFFFFu, ok && !*abort_flag)) break;
                 rows_to_slot(smem + SM_STAGING, smem + SM_STAGE + slot * kSlotBytes, live, lane);
                 // the slot is read by the tensor core; the staging buffer is refilled by bulk copies
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(B_FULL + slot));
-                if (j + 1 < n_tiles)
+                if (j + 1 < n_tiles) {
                     live = load_rows(p, sbase + SM_STAGING, bar(B_STAGE), sidx, staged, idx_base, b,
                                      start + (j + 1) * kTile, end, lane);
+                    issued = j + 2;
+                }
             }
+            // drain: at most the last staging load can still be landing
+            if (issued > 0) mbar_drain_wait(bar(B_STAGE), (issued - 1) & 1);
         } else if (lane == 0) {
-            for (int j = 0; j < kSlots && j < n_tiles; ++j)
+            int issued = 0;   // tiles loaded; tile j completes phase j / kSlots of slot j % kSlots
+            for (int j = 0; j < kSlots && j < n_tiles; ++j) {
                 load_tile(p, &tm_codes, &tm_scales, sbase, bar(B_FULL + j), sidx, staged, idx_base, b,
                           start + j * kTile, end, j);
+                issued = j + 1;
+            }
 #pragma unroll 1
             for (int i = 0; i + kSlots < n_tiles; ++i) {
                 const int slot = i % kSlots;
                 const uint32_t sph = (i / kSlots) & 1;
-                mbar_wait(bar(B_FREE + slot), sph, abort_flag, p.err);
-                mbar_wait(bar(B_QKD + slot), sph, abort_flag, p.err);
+                const bool f = mbar_wait(bar(B_FREE + slot), sph, abort_flag, p.err);
+                const bool d = mbar_wait(bar(B_QKD + slot), sph, abort_flag, p.err);
+                // after an abort nothing more is issued: a slot is re-armed only once its last
+                // transfer was consumed (the drain below waits for what is in flight)
+                if (!f || !d || *abort_flag) break;
                 fence_proxy_async_smem();
                 load_tile(p, &tm_codes, &tm_scales, sbase, bar(B_FULL + slot), sidx, staged, idx_base, b,
                           start + (i + kSlots) * kTile, end, slot);
+                issued = i + kSlots + 1;
             }
+            for (int j = issued > kSlots ? issued - kSlots : 0; j < issued; ++j)
+                mbar_drain_wait(bar(B_FULL + j % kSlots), (j / kSlots) & 1);
         }
+        // the Q image copy lands before the CTA can exit
+        if (lane == 0) mbar_drain_wait(bar(B_Q), 0);
         __syncwarp();
     } else if (warp == kMmaWarp) {
         // ============================================================ MMA issue
@@ -577,6 +600,10 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
                 }
             }
         }
+        // every MMA of this CTA completes before its TMEM is freed, on the abort path too
+        if (elect_one()) tc_commit(bar(B_DRAIN));
+        __syncwarp();
+        mbar_drain_wait(bar(B_DRAIN), 0);
     } else if (warp > kMmaWarp) {
         // ============================================================ producers: V chunks
         // lane -> token tq = lane & 15 of the chunk; 16-byte code chunks (32 dims) sc0 =

@@ -146,6 +146,12 @@ int nvfp4kv_mla_decode_plan(int batch, int q_len, int num_heads, int max_seq_len
  * hook clears itself.  Both NULL clears it. */
 int nvfp4kv_set_kernel_events(void* start, void* stop);
 
+/* Failure-detection self-test, no counterpart in the reference: one thread waits, with the
+ * bounded wait every kernel of this library uses, on an mbarrier that nothing arrives on.
+ * The wait gives up after its time limit (2 s) and ORs NVFP4KV_DEVERR_TIMEOUT into *err_flag;
+ * the kernel then returns normally, so the CUDA context stays usable. */
+int nvfp4kv_selftest_bounded_wait(int32_t* err_flag, nvfp4kv_stream_t stream);
+
 /* Capacity of the device scratch array behind nvfp4kv_mla_decode_static. */
 #define NVFP4KV_STATIC_SCRATCH_BYTES 33554432u
 

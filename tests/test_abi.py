@@ -21,7 +21,7 @@ def declared_functions():
 def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     names = declared_functions()
-    assert len(names) == 10, names
+    assert len(names) == 11, names
     for n in names:
         assert hasattr(lib, n), n
     assert set(names) == set(_lib.SIGNATURES)
@@ -100,6 +100,7 @@ def test_decode_plan():
     assert lib.nvfp4kv_mla_decode_plan(1, 0, 64, 8192, 0, ctypes.byref(splits), ctypes.byref(launches)) == _lib.EINVAL
     assert lib.nvfp4kv_set_kernel_events(None, None) == _lib.OK
     assert lib.nvfp4kv_set_kernel_events(ctypes.c_void_p(1), None) == _lib.EINVAL
+    assert lib.nvfp4kv_selftest_bounded_wait(None, None) == _lib.EINVAL   # checked before any launch
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
