@@ -183,6 +183,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
+// Per-warpgroup register budget (setmaxnreg): every thread of the 4 warps of a warpgroup runs
+// the same call.  An increase waits until other warpgroups of the CTA have released enough:
+// the budgets of all warpgroups must add up to no more than the block was launched with.
+template <uint32_t kRegs>
+__device__ __forceinline__ void warpgroup_reg_alloc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void warpgroup_reg_dealloc() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
 // Wait for a phase whatever the abort flag says, still bounded: run before a CTA exits so that
 // no bulk copy or tensor-core operation it issued is still writing its shared or tensor
 // memory, on the abort path too.

@@ -50,12 +50,18 @@ constexpr int kChunk = 16;                        // tokens per V chunk = PV K
 constexpr int kChunks = kTile / kChunk;           // 8
 constexpr int kSlots = 3;                         // tile ring depth (dense; sparse uses 2 + staging)
 constexpr int kVBufs = 2;                         // V chunk buffers
-constexpr int kSoftmaxWarps = 8;                  // 2 per TMEM sub-partition, 32 query rows each
-constexpr int kMmaWarp = 8;
-constexpr int kProducerWarps = 4;                 // warps 9-12: V chunks
-constexpr int kTmaWarp = 13;                      // lane 0 issues every TMA / bulk load
-constexpr int kThreads = (kTmaWarp + 1) * 32;     // 448
+// Four warpgroups.  Registers are moved between them at run time (setmaxnreg): the block is
+// launched with 128 per thread; softmax takes 168, producers keep 96, the control group 80.
+constexpr int kSoftmaxWarps = 8;                  // warpgroups 0-1: 2 per TMEM sub-partition, 32 rows each
+constexpr int kProducerWarp0 = 8;                 // warpgroup 2: V chunks and the pool scale factors
+constexpr int kProducerWarps = 4;
+constexpr int kMmaWarp = 12;                      // warpgroup 3: MMA issue,
+constexpr int kTmaWarp = 13;                      //   every TMA / bulk load, and two spare warps
+constexpr int kThreads = 16 * 32;                 // 512
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
+constexpr uint32_t kRegsSoftmax = 168, kRegsProducer = 96, kRegsCtl = 80;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsProducer + 128 * kRegsCtl == kThreads * 128,
+              "the register split uses exactly what the block is launched with");
 constexpr float kRescaleLog2 = 8.0f;
 
 // Shared memory map (offsets from a 1024-byte aligned base).
@@ -75,7 +81,8 @@ constexpr int SM_LSUM = SM_LIM + 256;                     // 64 f32: row sums
 constexpr int SM_RED = SM_LSUM + 256;                     // 4 sub-partitions x 64 f32
 constexpr int SM_ROWOFF = SM_RED + 4 * 64 * 4;            // 64 i64: output row offsets
 constexpr int SM_FLAGS = SM_ROWOFF + 64 * 8;              // [0] TMEM base, [1] abort
-constexpr int SM_BARS = SM_FLAGS + 16;
+constexpr int SM_TMASK = SM_FLAGS + 16;                   // kSlots x 4 words: tile rows that are valid
+constexpr int SM_BARS = SM_TMASK + kSlots * 16;
 enum {
     B_FULL = 0,                    // [kSlots] raw tile landed (TMA transaction bytes)
     B_FREE = B_FULL + kSlots,      // [kSlots] producers finished reading the slot
@@ -210,27 +217,50 @@ __device__ __forceinline__ int page_id(const Fp4Params& p, const int* sidx, bool
 // TMA loads of tile `tile_start` into ring slot `slot`.  Every box is issued (a missing page
 // or a box past the context is addressed out of range and reads as zeros), so the slot always
 // receives kSlotBytes.
+// Rows [lo, hi) of a tile -> bits of a 128-bit row mask.
+__device__ __forceinline__ void mask_rows(uint32_t (&m)[4], int lo, int hi) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        const int a = max(lo, 32 * w), e = min(hi, 32 * w + 32);
+        if (a < e) m[w] |= (e - a == 32 ? 0xFFFFFFFFu : ((1u << (e - a)) - 1u)) << (a - 32 * w);
+    }
+}
+
+// TMA loads of tile `tile_start` into ring slot `slot`.  Every box is issued (a missing page
+// or a box past the context is addressed out of range and reads as zeros), so the slot always
+// receives kSlotBytes.  The tile's valid rows (in range, on a valid page) go to `mask` first,
+// published to the slot's waiters by the barrier arrival.
 __device__ __forceinline__ void load_tile(const Fp4Params& p, const void* tm_codes, const void* tm_scales,
                                           uint32_t sbase, uint32_t bar_full, const int* sidx, bool staged,
-                                          int idx_base, int b, int tile_start, int end, int slot) {
-    mbar_arrive_expect_tx(bar_full, kSlotBytes);
+                                          int idx_base, int b, int tile_start, int end, int slot,
+                                          uint32_t* mask) {
     const int box = p.box_rows;
+    int y[kTile / 16];
+    uint32_t m[4] = {0u, 0u, 0u, 0u};
+#pragma unroll 1
+    for (int r0 = 0, k = 0; r0 < kTile; r0 += box, ++k) {
+        const int pos = tile_start + r0;
+        y[k] = -box;
+        if (pos < end) {
+            const int pg = page_id(p, sidx, staged, idx_base, b, pos);
+            if (pg >= 0 && pg < p.num_pages) {
+                y[k] = (pg << p.page_shift) | (pos & ((1 << p.page_shift) - 1));
+                mask_rows(m, r0, min(r0 + box, end - tile_start));
+            } else {
+                set_error(p.err, NVFP4KV_DEVERR_BAD_PAGE);
+            }
+        }
+    }
+#pragma unroll
+    for (int w = 0; w < 4; ++w) mask[w] = m[w];
+    mbar_arrive_expect_tx(bar_full, kSlotBytes);
     const uint32_t codes = sbase + SM_STAGE + slot * kSlotBytes;
     const uint32_t scales = codes + kCodeBytes;
 #pragma unroll 1
-    for (int r0 = 0; r0 < kTile; r0 += box) {
-        const int pos = tile_start + r0;
-        int y = -box;
-        if (pos < end) {
-            const int pg = page_id(p, sidx, staged, idx_base, b, pos);
-            if (pg >= 0 && pg < p.num_pages)
-                y = (pg << p.page_shift) | (pos & ((1 << p.page_shift) - 1));
-            else
-                set_error(p.err, NVFP4KV_DEVERR_BAD_PAGE);
-        }
-        tma_load_2d(codes + r0 * 128, tm_codes, 0, y, bar_full);
-        tma_load_2d(codes + 16384 + r0 * 128, tm_codes, 128, y, bar_full);
-        tma_load_2d(scales + r0 * 32, tm_scales, 256, y, bar_full);
+    for (int r0 = 0, k = 0; r0 < kTile; r0 += box, ++k) {
+        tma_load_2d(codes + r0 * 128, tm_codes, 0, y[k], bar_full);
+        tma_load_2d(codes + 16384 + r0 * 128, tm_codes, 128, y[k], bar_full);
+        tma_load_2d(scales + r0 * 32, tm_scales, 256, y[k], bar_full);
     }
 }
 
@@ -434,6 +464,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
     float* red = reinterpret_cast<float*>(smem + SM_RED);
     int64_t* rowoff = reinterpret_cast<int64_t*>(smem + SM_ROWOFF);
     int* sidx = reinterpret_cast<int*>(smem + SM_IDX);
+    uint32_t* tmask = reinterpret_cast<uint32_t*>(smem + SM_TMASK);   // [slot][4]: valid rows
     volatile int* flags = reinterpret_cast<volatile int*>(smem + SM_FLAGS);
     volatile int* abort_flag = flags + 1;
     auto bar = [&](int i) -> uint32_t { return sbase + SM_BARS + 8 * i; };
@@ -475,6 +506,8 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
     tc_fence_after();
     const uint32_t tmem = static_cast<uint32_t>(flags[0]);
 
+    if (warp >= kMmaWarp) {
+    warpgroup_reg_dealloc<kRegsCtl>();
     if (warp == kTmaWarp) {
         // ============================================================ TMA / bulk loads
         if (lane == 0) {
@@ -508,6 +541,11 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
                 // after an abort nothing more is issued (the drain below waits for what was)
                 if (!__all_sync(0xFFFFFFFFu, ok && !*abort_flag)) break;
                 rows_to_slot(smem + SM_STAGING, smem + SM_STAGE + slot * kSlotBytes, live, lane);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t w = __ballot_sync(0xFFFFFFFFu, (live >> k) & 1u);
+                    if (lane == 0) tmask[4 * slot + k] = w;
+                }
                 // the slot is read by the tensor core; the staging buffer is refilled by bulk copies
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -524,7 +562,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             int issued = 0;   // tiles loaded; tile j completes phase j / kSlots of slot j % kSlots
             for (int j = 0; j < kSlots && j < n_tiles; ++j) {
                 load_tile(p, &tm_codes, &tm_scales, sbase, bar(B_FULL + j), sidx, staged, idx_base, b,
-                          start + j * kTile, end, j);
+                          start + j * kTile, end, j, tmask + 4 * j);
                 issued = j + 1;
             }
 #pragma unroll 1
@@ -538,7 +576,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
                 if (!f || !d || *abort_flag) break;
                 fence_proxy_async_smem();
                 load_tile(p, &tm_codes, &tm_scales, sbase, bar(B_FULL + slot), sidx, staged, idx_base, b,
-                          start + (i + kSlots) * kTile, end, slot);
+                          start + (i + kSlots) * kTile, end, slot, tmask + 4 * slot);
                 issued = i + kSlots + 1;
             }
             for (int j = issued > kSlots ? issued - kSlots : 0; j < issued; ++j)
@@ -604,11 +642,32 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
         if (elect_one()) tc_commit(bar(B_DRAIN));
         __syncwarp();
         mbar_drain_wait(bar(B_DRAIN), 0);
-    } else if (warp > kMmaWarp) {
+    }
+    } else if (warp >= kProducerWarp0) {
+        warpgroup_reg_dealloc<kRegsProducer>();
         // ============================================================ producers: V chunks
         // lane -> token tq = lane & 15 of the chunk; 16-byte code chunks (32 dims) sc0 =
-        // 4 pw + (lane >> 4) and sc0 + 2
-        const int pw = warp - kMmaWarp - 1;
+        // 4 pw + (lane >> 4) and sc0 + 2.  Sparse: warp pw also writes the pool scales of each
+        // tile (A scale factors) into its TMEM sub-partition pw, one tile ahead of QK (dense
+        // tiles land early, so the softmax warps do it there, off the V-chunk chain).
+        const int pw = warp - kProducerWarp0;
+        const uint32_t lane_base = static_cast<uint32_t>(32 * pw) << 16;
+        // scales of tile j -> TMEM slot j & 1.  Its last reader, QK(j-2), is complete: the
+        // producers reach tile j-1 only after PV(j-2) chunk 5, which the tensor core runs
+        // after QK(j-1).
+        auto write_sfa = [&](int j) {
+            const int sl = j % kRing;
+            mbar_wait(bar(B_FULL + sl), (j / kRing) & 1, abort_flag, p.err);
+            tc_fence_after();
+            scales_to_tmem(smem + SM_STAGE + sl * kSlotBytes + kCodeBytes, tmem + kTSFA + 32 * (j & 1) + lane_base, lane);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_SFA_FULL + (j & 1)));
+        };
+        // a sparse tile is rearranged into its slot only once the slot's previous tile is
+        // done: give that two chunks of time before the next tile's scales are written
+        constexpr int kSfaChunk = 2;
+        if (kSparse && n_tiles > 0) write_sfa(0);
 #pragma unroll 1
         for (int i = 0; i < n_tiles; ++i) {
             const int slot = i % kRing;
@@ -617,6 +676,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             const uint8_t* scales = codes + kCodeBytes;
 #pragma unroll 1
             for (int c = 0; c < kChunks; ++c) {
+                if (kSparse && c == kSfaChunk && i + 1 < n_tiles) write_sfa(i + 1);
                 const int u = kChunks * i + c, vb = u % kVBufs;
                 const int tq = lane & 15;
                 const int tok = c * kChunk + tq;
@@ -661,6 +721,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             if (lane == 0) mbar_arrive(bar(B_FREE + slot));
         }
     } else {
+        warpgroup_reg_alloc<kRegsSoftmax>();
         // ============================================================ softmax
         // warp w: TMEM sub-partition sp = w & 3 (token t = 32 sp + lane), query rows 32 hh .. +32
         const int sp = warp & 3, hh = warp >> 2;
@@ -696,7 +757,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             tmem_st32(tmem + kTSFB + 32 * hh + lane_base, rr);
             tmem_wait_st();
         }
-        if (hh == 0 && n_tiles > 0) {
+        if (!kSparse && hh == 0 && n_tiles > 0) {
             mbar_wait(bar(B_FULL + 0), 0, abort_flag, p.err);
             scales_to_tmem(smem + SM_STAGE + kCodeBytes, tmem + kTSFA + lane_base, lane);
             tc_fence_before();
@@ -712,9 +773,9 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
         for (int i = 0; i < n_tiles; ++i) {
             mbar_wait(bar(B_S_FULL), i & 1, abort_flag, p.err);
             tc_fence_after();
-            // pool scales of tile i+1 -> its TMEM slot (QK(i-1), the slot's last reader, is
-            // complete: S_FULL(i) tracks every earlier MMA)
-            if (hh == 0 && i + 1 < n_tiles) {
+            // dense: pool scales of tile i+1 -> its TMEM slot (QK(i-1), the slot's last reader,
+            // is complete: S_FULL(i) tracks every earlier MMA)
+            if (!kSparse && hh == 0 && i + 1 < n_tiles) {
                 const int slot1 = (i + 1) % kRing;
                 mbar_wait(bar(B_FULL + slot1), ((i + 1) / kRing) & 1, abort_flag, p.err);
                 scales_to_tmem(smem + SM_STAGE + slot1 * kSlotBytes + kCodeBytes,
@@ -724,21 +785,26 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
                 if (lane == 0) mbar_arrive(bar(B_SFA_FULL + ((i + 1) & 1)));
             }
 
-            float sraw[32];
-            {
+            // Scores of this thread's token for its 32 query rows (S^T stays allocated until
+            // the vote below: a rescale reads it again).
+            float sv[32];
+            auto load_scores = [&]() {
                 uint32_t a[32], c2[32];
                 tmem_ld32(tmem + kTS + 32 * hh + lane_base, a);
                 tmem_ld32(tmem + kTS + 64 + 32 * hh + lane_base, c2);
                 tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) sraw[j] = __uint_as_float(a[j]) + __uint_as_float(c2[j]);
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(B_S_FREE));
+                for (int j = 0; j < 32; ++j) sv[j] = __uint_as_float(a[j]) + __uint_as_float(c2[j]);
+            };
+            load_scores();
             const int pos = start + i * kTile + t;
-            const bool tok_ok = pos < end && token_row<kSparse>(p, sidx, staged, idx_base, b, pos, false) >= 0;
-            // does any visible score exceed its row's running max by more than 2^8?
+            // valid row of the tile: the load warp publishes the mask with the slot's barrier
+            // (complete long before S^T of the tile exists, and not re-armed before P(i))
+            mbar_wait(bar(B_FULL + i % kRing), (i / kRing) & 1, abort_flag, p.err);
+            const bool tok_ok = (tmask[4 * (i % kRing) + (t >> 5)] >> (t & 31)) & 1u;
+            // Probabilities against the running row maxima, computed speculatively in place:
+            // p = 2^(s qs - m).  They stand unless some visible score exceeds its row's max by
+            // more than 2^8 (a vote over the CTA); then the maxima move and p is recomputed.
             bool grow = false;
 #pragma unroll
             for (int n4 = 0; n4 < 8; ++n4) {
@@ -751,13 +817,22 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     const bool vis = tok_ok && (!per_row_lim || pos < lv[k]);
-                    grow |= vis && fmaf(sraw[4 * n4 + k], qv[k], -mv[k]) > kRescaleLog2;
+                    const float x = fmaf(sv[4 * n4 + k], qv[k], -mv[k]);
+                    grow |= vis && x > kRescaleLog2;
+                    sv[4 * n4 + k] = vis ? ex2_approx(x) : 0.0f;
                 }
             }
             const bool any = named_bar_red_or(1, kSoftmaxThreads, grow);
             uint32_t pk[16];
-            if (any) {
+            if (!any) {
+                // common case: P is ready before PV(i-1) completes
+#pragma unroll
+                for (int n = 0; n < 32; ++n) l[n] += sv[n];
+#pragma unroll
+                for (int k = 0; k < 16; ++k) pk[k] = pack_half2(sv[2 * k], sv[2 * k + 1]);
+            } else {
                 // new row max = max(old, tile max); alpha = 2^(old - new)
+                load_scores();
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {   // 16 rows at a time keeps the register count down
                     float xv[16];
@@ -770,7 +845,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
                             const bool vis = tok_ok && (!per_row_lim || pos < lv[k]);
-                            xv[4 * n4 + k] = vis ? sraw[16 * hf + 4 * n4 + k] * qv[k] : -INFINITY;
+                            xv[4 * n4 + k] = vis ? sv[16 * hf + 4 * n4 + k] * qv[k] : -INFINITY;
                         }
                     }
                     const float mx = warp_max_scatter16(xv, lane);
@@ -794,10 +869,11 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
                     l[4 * n4 + 2] *= a4.z;
                     l[4 * n4 + 3] *= a4.w;
                 }
-            } else {
-                // common case: the maxima stand, so P is ready before PV(i-1) completes
-                probs32(sraw, qs_h, M_h, lim_h, tok_ok, per_row_lim, pos, l, pk);
             }
+            // S^T is no longer needed (QK(i+1) may overwrite it)
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_S_FREE));
             if (i > 0) {
                 // P^T is single-buffered and O^T must be stable: wait for PV(i-1).  QK(i+1) is
                 // queued on the tensor core ahead of PV(i), so the work below stays hidden.
@@ -819,7 +895,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
                     tmem_wait_st();
                 }
             }
-            if (any) probs32(sraw, qs_h, M_h, lim_h, tok_ok, per_row_lim, pos, l, pk);
+            if (any) probs32(sv, qs_h, M_h, lim_h, tok_ok, per_row_lim, pos, l, pk);
             // P^T row t, 16-byte chunks 4hh .. 4hh+3 (rows 32hh .. 32hh+31), 128-byte swizzled
             uint8_t* prow = smem + SM_PT + t * 128;
 #pragma unroll
