@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Benchmark of the NVFP4 paged KV-cache read path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dense8k|dense128k|sparse]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dense8k|dense128k|sparse|long]
                     [--impl ours|reference]
 
 Default workload = BASELINE config 2: dense MLA decode over the 288-byte NVFP4 paged pool,
@@ -46,6 +46,11 @@ WORKLOADS = {
     "sparse": dict(desc="config 3: sparse top-2048 decode, batch 16, 64 heads, 128K-token "
                         "sequences on shuffled pages, indices drawn without replacement",
                    B=16, H=64, QL=1, ctx=131072, topk=2048),
+    # config 4 per layer: 5 x 460,000 + 3 x 900,000 tokens, MTP q_len 3, split over the ranks
+    # by the token-balanced sequence partition (strong scaling: the job is fixed)
+    "long": dict(desc="config 4 (one layer): 5 x 460,000 + 3 x 900,000-token sequences, 64 heads, "
+                      "MTP q_len 3, token-balanced sequence / page-range partition over the ranks",
+                 B=8, H=64, QL=3, ctx=0, topk=0, lens=[460000] * 5 + [900000] * 3),
 }
 
 
@@ -178,8 +183,214 @@ def make_layers(rt, torch, wl, layers, dev, seed):
 
 
 def kv_bytes_per_step(wl) -> int:
+    if "lens" in wl:
+        return sum(wl["lens"]) * NV_BYTES
     rows = wl["B"] * (wl["topk"] if wl["topk"] else wl["ctx"])
     return rows * NV_BYTES
+
+
+# pieces per rank of the long workload: one call's split plan is uniform over its units, so
+# the rank's tokens are cut into this many equal ranges (40 x 3 query groups fill 120-144 SMs)
+LONG_PIECES_PER_RANK = 40
+
+
+def make_long_step(rt, torch, wl, dev, rank, world, seed):
+    """The partitioned long-context step on this rank: its pieces' pages written by the append
+    kernel into a rank-local pool, two decode calls (pieces before a sequence's causal tail
+    with q_len folded into the heads; tails with the causal limit) and the exact log-sum-exp
+    merge of the pieces into per-sequence partial results.  Returns (step_fn, state)."""
+    from glm53_flash_dual_dgx_spark_b200 import partition as P
+
+    lens, QL, H = wl["lens"], wl["QL"], wl["H"]
+    plan = P.plan(lens, world * LONG_PIECES_PER_RANK, 64, q_len=QL)
+    units = [u for part in plan[rank * LONG_PIECES_PER_RANK:(rank + 1) * LONG_PIECES_PER_RANK] for u in part]
+    pages = [(u.tokens + 63) // 64 for u in units]
+    pool = torch.empty(sum(pages), 64, NV_BYTES, dtype=torch.uint8, device=dev)
+    torch.manual_seed(seed)
+    for c in range(0, pool.shape[0] * 64, 1 << 20):
+        n = min(1 << 20, pool.shape[0] * 64 - c)
+        rt.write_nvfp4(torch.randn(n, 512, device=dev).to(torch.bfloat16), pool, torch.arange(c, c + n, device=dev))
+    g = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(pool.shape[0], generator=g).to(torch.int32)
+    tables, k = [], 0
+    for m in pages:
+        tables.append(perm[k:k + m])
+        k += m
+    q = torch.randn(len(lens), QL, H, 576, generator=g).to(torch.bfloat16).to(dev)
+    calls = []
+    for last in (False, True):
+        idx = [i for i, u in enumerate(units) if u.last == last]
+        if not idx:
+            continue
+        width = max(tables[i].numel() for i in idx)
+        tb = torch.full((len(idx), width), -1, dtype=torch.int32)
+        for row, i in enumerate(idx):
+            tb[row, :tables[i].numel()] = tables[i]
+        sl = torch.tensor([units[i].tokens for i in idx], dtype=torch.int32)
+        seqs = torch.tensor([units[i].seq for i in idx], dtype=torch.long, device=dev)
+        n = len(idx)
+        fold = not last and QL > 1
+        calls.append(dict(idx=torch.tensor(idx, dtype=torch.long, device=dev), seqs=seqs, tables=tb.to(dev),
+                          seq=sl.to(dev), max_len=int(sl.max()), fold=fold, n=n,
+                          qbuf=torch.empty(n, QL, H, 576, dtype=torch.bfloat16, device=dev),
+                          out=torch.empty(n, QL, H, 512, dtype=torch.bfloat16, device=dev)))
+    U = len(units)
+    out_u = torch.empty(U, QL, H, 512, dtype=torch.bfloat16, device=dev)
+    lse_u = torch.empty(U, QL, H, dtype=torch.float32, device=dev)
+    seq_of = torch.tensor([u.seq for u in units], dtype=torch.long, device=dev)
+    sm = 1.0 / math.sqrt(576)
+    state = dict(units=units, plan=plan, pool=pool, q=q, out=None, lse=None, out_u=out_u, lse_u=lse_u,
+                 calls=calls)
+
+    def step():
+        for c in calls:
+            torch.index_select(q, 0, c["seqs"], out=c["qbuf"])
+            qq = c["qbuf"].view(c["n"], 1, QL * H, 576) if c["fold"] else c["qbuf"]
+            oo = c["out"].view(c["n"], 1, QL * H, 512) if c["fold"] else c["out"]
+            o, l = rt.mla_decode_lse(qq, pool, None, 128, 512, 64, c["tables"], c["seq"], c["max_len"],
+                                     out=oo, bmm1_scale=sm, bmm2_scale=1.0)
+            out_u[c["idx"]] = c["out"]
+            lse_u[c["idx"]] = l.view(c["n"], QL, H)
+        state["out"], state["lse"] = P.merge(out_u, lse_u, seq_of, len(lens))
+
+    return step, state, sum(u.tokens for u in units) * NV_BYTES
+
+
+def run_long(args, wl, rt, torch, dist, dev, rank, world, local):
+    """--workload long: the partitioned config-4 layer (strong scaling)."""
+    from glm53_flash_dual_dgx_spark_b200 import partition as P
+
+    step, st, rank_bytes = make_long_step(rt, torch, wl, dev, rank, world, seed=1)
+    job_bytes = kv_bytes_per_step(wl)
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(gr, stream=s):
+            step()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    launches = 0
+    for c in st["calls"]:
+        qlen, heads = (1, wl["QL"] * wl["H"]) if c["fold"] else (wl["QL"], wl["H"])
+        launches += rt.mla_decode_plan(c["n"], qlen, heads, c["max_len"], 0, dev)[1]
+    sampler = ClockSampler(local)
+    sampler.start()
+    soak_end = time.perf_counter() + 1.0
+    k = 0
+    while time.perf_counter() < soak_end or k < args.warmup:
+        gr.replay()
+        k += 1
+        if k % 16 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        gr.replay()
+    ev1.record()
+    ev1.synchronize()
+    t1 = time.perf_counter()
+    if world > 1:
+        dist.barrier()
+    sampler.stop()
+    t_max = torch.tensor([ev0.elapsed_time(ev1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms_max = float(t_max.item())
+    value = job_bytes * args.steps / (ms_max / 1e3) / 1e9
+
+    # end to end through the public API: q host->device, the rank's decode + merge, the rank's
+    # merged partial outputs device->host (eager)
+    q_h = st["q"].cpu().pin_memory()
+    out_h = torch.empty(wl["B"], wl["QL"], wl["H"], 512, dtype=torch.bfloat16).pin_memory()
+    e_steps = max(10, min(args.e2e_steps, 50))
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e_steps):
+        st["q"].copy_(q_h, non_blocking=True)
+        step()
+        out_h.copy_(st["out"], non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = job_bytes * e_steps / (float(e_ms.item()) / 1e3) / 1e9
+
+    # the dominant attention kernel alone (the pieces before each causal tail), events
+    # recorded by the library around it
+    big = max(st["calls"], key=lambda c: c["n"])
+    big_bytes = int(big["seq"].sum().item()) * NV_BYTES
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(10)]
+    sm = 1.0 / math.sqrt(576)
+    for a, b in kev:
+        qq = big["qbuf"].view(big["n"], 1, wl["QL"] * wl["H"], 576) if big["fold"] else big["qbuf"]
+        oo = big["out"].view(big["n"], 1, wl["QL"] * wl["H"], 512) if big["fold"] else big["out"]
+        rt.set_kernel_events(a, b)
+        rt.mla_decode_lse(qq, st["pool"], None, 128, 512, 64, big["tables"], big["seq"], big["max_len"],
+                          out=oo, bmm1_scale=sm)
+    torch.cuda.synchronize()
+    kernel_ms = sum(a.elapsed_time(b) for a, b in kev) / len(kev)
+    k_ms = torch.tensor([kernel_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(k_ms, op=dist.ReduceOp.MAX)
+    kernel_ms = float(k_ms.item())
+
+    # after timing: the cross-rank merge (the only data collective)
+    if world > 1:
+        out_u, lse_u = st["out_u"], st["lse_u"]
+        P.gather_merge(out_u, lse_u, [[u for part in st["plan"][r * LONG_PIECES_PER_RANK:(r + 1) * LONG_PIECES_PER_RANK]
+                                       for u in part] for r in range(world)], rank, wl["B"])
+        torch.cuda.synchronize()
+    errors = rt.device_errors(dev)
+    if rank == 0:
+        peak, peak_kind = load_peaks()
+        achieved = big_bytes / (kernel_ms / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded N(0,1) latent quantised by the append kernel; N(0,1) q)",
+            "config": {"workload": wl["desc"], "global_batch": wl["B"], "seq_len": max(wl["lens"]),
+                       "tokens": sum(wl["lens"]), "heads": wl["H"], "q_len": wl["QL"],
+                       "pieces_per_rank": LONG_PIECES_PER_RANK, "units_on_rank0": len(st["units"]),
+                       "l2": f"inputs larger than L2: {rank_bytes / 2**20:.0f} MiB read per step on rank 0",
+                       "parallelism": f"sequence / page-range partition x{world} (strong scaling)"},
+            "decode_tokens_per_s": round(wl["B"] * wl["QL"] * args.steps / (ms_max / 1e3), 1),
+            "kv_rows_per_s": round(job_bytes * args.steps / (ms_max / 1e3) / NV_BYTES, 1),
+            "hbm_frac_of_8tbs": round(value / world / 8000.0, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                         "per_launch_bytes": big_bytes, "kernel_ms": round(kernel_ms, 5),
+                         "kernel": "decode_fp4_kernel<dense>",
+                         "step_frac_in_kernel": round(kernel_ms / (ms_max / args.steps), 3)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": q_h.numel() * 2,
+                    "d2h_bytes_per_step": out_h.numel() * 2, "steps": e_steps},
+            "gpu_launches": args.steps * launches,
+            "clocks": sampler.summary(t0, t1),
+            "device_errors": errors,
+        }
+        if world == 1:
+            gbs, per, ctx = cpu_decode_sample(wl, args.cpu_seconds)
+            line["cpu_baseline"] = {
+                "value": round(gbs, 4), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+                "sample": f"oracle decode of one {ctx}-token piece x {wl['QL']} x {wl['H']} query rows "
+                          f"repeated for ~{args.cpu_seconds:.0f} s ({per * 1e3:.1f} ms each; {cpu_model()})"}
+        print(json.dumps(line), flush=True)
+    del gr
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 # ---------------------------------------------------------------------------- CPU side
@@ -191,7 +402,7 @@ def cpu_decode_sample(wl, seconds: float):
 
     from oracle import oracle as O
 
-    ctx = wl["topk"] if wl["topk"] else min(wl["ctx"], 8192)
+    ctx = wl["topk"] if wl["topk"] else min(wl["ctx"] or 8192, 8192)
     g = torch.Generator().manual_seed(11)
     x = torch.randn(ctx, 512, generator=g).to(torch.bfloat16)
     pool = O.quant_new(x)
@@ -236,7 +447,8 @@ def reference_arm(args, wl):
             "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) latent and q)",
             "config": {"workload": wl["desc"], "global_batch": wl["B"] * args.gpus,
-                       "seq_len": wl["topk"] or wl["ctx"], "parallelism": f"sequence-partitioned x{args.gpus}"},
+                       "seq_len": wl["topk"] or wl["ctx"] or max(wl.get("lens", [0])),
+                       "parallelism": f"sequence-partitioned x{args.gpus}"},
             "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -276,6 +488,9 @@ def main() -> None:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    if "lens" in wl:
+        run_long(args, wl, rt, torch, dist, dev, rank, world, local)
+        return
 
     kvb = kv_bytes_per_step(wl)
     # layers so that one rotation reads more than L2 (sparse: distinct top-k sets)

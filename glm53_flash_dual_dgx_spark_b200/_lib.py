@@ -37,6 +37,11 @@ SIGNATURES = {
                                 _P, _I64, _I64, _I64,          # out + strides
                                 _P, _SZ,                       # workspace
                                 _P, _P]),                      # err_flag, stream
+    "nvfp4kv_mla_decode_lse": (_I, [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P,
+                                    _I, _I, _I, _I, _I, _I, _I, _I, _F, _F,
+                                    _P, _I64, _I64, _I64,
+                                    _P,                         # lse
+                                    _P, _SZ, _P, _P]),          # workspace, err_flag, stream
     "nvfp4kv_mla_decode_workspace_size": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_SZ)]),
     "nvfp4kv_mla_decode_plan": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
     "nvfp4kv_set_kernel_events": (_I, [_P, _P]),

@@ -41,6 +41,7 @@ struct DecodeArgs {
     float* part_o;    // [splits][batch][groups][64][512] when splits > 1
     float* part_ml;   // [splits][batch][groups][64][2]
     uint8_t* qimg;    // [batch][groups][kQImageBytes]
+    float* lse;       // optional [batch][q_len][heads]: natural-log sum of exp(bmm1_scale q.k)
     int32_t* err;
 };
 

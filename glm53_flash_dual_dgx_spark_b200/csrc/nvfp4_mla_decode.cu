@@ -30,7 +30,8 @@ constexpr int kMaxSplits = kDecMaxSplits;
 __global__ void __launch_bounds__(128)
 combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int splits,
                int batch, int groups, int q_len, int num_heads, float bmm2_scale,
-               __nv_bfloat16* __restrict__ out, int64_t o_sb, int64_t o_sq, int64_t o_sh) {
+               __nv_bfloat16* __restrict__ out, int64_t o_sb, int64_t o_sq, int64_t o_sh,
+               float* __restrict__ lse) {
     __shared__ float wts[kMaxSplits];
     const int n = blockIdx.x % kNQ;
     const int bg = blockIdx.x / kNQ;
@@ -65,6 +66,10 @@ combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) Ls += __shfl_xor_sync(0xFFFFFFFFu, Ls, o);
         const float inv = Ls > 0.0f ? bmm2_scale / Ls : 0.0f;
+        // log-sum-exp of the row's scores over all splits: sum 2^x = 2^M Ls (x in log2 units)
+        if (lse && lane == 0)
+            lse[static_cast<int64_t>(b) * q_len * num_heads + r] =
+                Ls > 0.0f ? 0.69314718055994531f * (M + log2f(Ls)) : -INFINITY;
 #pragma unroll
         for (int k = 0; k < 2; ++k)
             if (lane + 32 * k < splits) wts[lane + 32 * k] = w[k] * inv;
@@ -163,17 +168,16 @@ extern "C" int nvfp4kv_mla_decode_plan(int batch, int q_len, int num_heads, int 
     return NVFP4KV_OK;
 }
 
-extern "C" int nvfp4kv_mla_decode(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,
-                                  const uint8_t* pool, int64_t pool_rows,
-                                  const int32_t* tables, int64_t tables_stride,
-                                  const int32_t* seq_lens,
-                                  int batch, int q_len, int num_heads, int head_dim_qk, int kv_lora_rank,
-                                  int sparse_topk, int page_size, int max_seq_len,
-                                  float bmm1_scale, float bmm2_scale,
-                                  void* out, int64_t out_stride_b, int64_t out_stride_q, int64_t out_stride_h,
-                                  void* workspace, size_t workspace_bytes,
-                                  int32_t* err_flag, nvfp4kv_stream_t stream) {
-    using namespace nvfp4kv;
+namespace nvfp4kv {
+namespace {
+
+int decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,
+                const uint8_t* pool, int64_t pool_rows, const int32_t* tables, int64_t tables_stride,
+                const int32_t* seq_lens, int batch, int q_len, int num_heads, int head_dim_qk,
+                int kv_lora_rank, int sparse_topk, int page_size, int max_seq_len, float bmm1_scale,
+                float bmm2_scale, void* out, int64_t out_stride_b, int64_t out_stride_q,
+                int64_t out_stride_h, float* lse, void* workspace, size_t workspace_bytes,
+                int32_t* err_flag, nvfp4kv_stream_t stream) {
     if (batch < 0) return fail(NVFP4KV_EINVAL, "mla_decode: batch < 0");
     if (batch == 0) return NVFP4KV_OK;
     if (!q || !pool || !tables || !seq_lens || !out)
@@ -224,7 +228,7 @@ extern "C" int nvfp4kv_mla_decode(const void* q, int64_t q_stride_b, int64_t q_s
         a.max_seq_len = max_seq_len;
         a.bmm1_scale = bmm1_scale; a.bmm2_scale = bmm2_scale;
         a.out = out; a.o_sb = out_stride_b; a.o_sq = out_stride_q; a.o_sh = out_stride_h;
-        a.part_o = part_o; a.part_ml = part_ml; a.err = err_flag;
+        a.part_o = part_o; a.part_ml = part_ml; a.err = err_flag; a.lse = lse;
         a.qimg = static_cast<uint8_t*>(workspace) + pl.part_bytes;
         if ((rc = launch_decode_fp4(a, pl, st)) != NVFP4KV_OK) return rc;
     }
@@ -232,8 +236,45 @@ extern "C" int nvfp4kv_mla_decode(const void* q, int64_t q_stride_b, int64_t q_s
         combine_kernel<<<batch * pl.groups * kNQ, 128, 0, st>>>(part_o, part_ml, pl.splits, batch, pl.groups,
                                                           q_len, num_heads, bmm2_scale,
                                                           static_cast<__nv_bfloat16*>(out), out_stride_b,
-                                                          out_stride_q, out_stride_h);
+                                                          out_stride_q, out_stride_h, lse);
         if ((rc = check_launch("nvfp4kv_mla_decode combine")) != NVFP4KV_OK) return rc;
     }
     return NVFP4KV_OK;
+}
+
+}  // namespace
+}  // namespace nvfp4kv
+
+extern "C" int nvfp4kv_mla_decode(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,
+                                  const uint8_t* pool, int64_t pool_rows,
+                                  const int32_t* tables, int64_t tables_stride,
+                                  const int32_t* seq_lens,
+                                  int batch, int q_len, int num_heads, int head_dim_qk, int kv_lora_rank,
+                                  int sparse_topk, int page_size, int max_seq_len,
+                                  float bmm1_scale, float bmm2_scale,
+                                  void* out, int64_t out_stride_b, int64_t out_stride_q, int64_t out_stride_h,
+                                  void* workspace, size_t workspace_bytes,
+                                  int32_t* err_flag, nvfp4kv_stream_t stream) {
+    return nvfp4kv::decode_impl(q, q_stride_b, q_stride_q, q_stride_h, pool, pool_rows, tables, tables_stride,
+                                seq_lens, batch, q_len, num_heads, head_dim_qk, kv_lora_rank, sparse_topk,
+                                page_size, max_seq_len, bmm1_scale, bmm2_scale, out, out_stride_b,
+                                out_stride_q, out_stride_h, nullptr, workspace, workspace_bytes, err_flag,
+                                stream);
+}
+
+extern "C" int nvfp4kv_mla_decode_lse(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,
+                                      const uint8_t* pool, int64_t pool_rows,
+                                      const int32_t* tables, int64_t tables_stride,
+                                      const int32_t* seq_lens,
+                                      int batch, int q_len, int num_heads, int head_dim_qk, int kv_lora_rank,
+                                      int sparse_topk, int page_size, int max_seq_len,
+                                      float bmm1_scale, float bmm2_scale,
+                                      void* out, int64_t out_stride_b, int64_t out_stride_q, int64_t out_stride_h,
+                                      float* lse, void* workspace, size_t workspace_bytes,
+                                      int32_t* err_flag, nvfp4kv_stream_t stream) {
+    if (!lse) return nvfp4kv::fail(NVFP4KV_EINVAL, "mla_decode_lse: null lse");
+    return nvfp4kv::decode_impl(q, q_stride_b, q_stride_q, q_stride_h, pool, pool_rows, tables, tables_stride,
+                                seq_lens, batch, q_len, num_heads, head_dim_qk, kv_lora_rank, sparse_topk,
+                                page_size, max_seq_len, bmm1_scale, bmm2_scale, out, out_stride_b,
+                                out_stride_q, out_stride_h, lse, workspace, workspace_bytes, err_flag, stream);
 }

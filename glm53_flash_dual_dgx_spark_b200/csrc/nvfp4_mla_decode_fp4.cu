@@ -130,6 +130,7 @@ struct Fp4Params {
     float* part_o;
     float* part_ml;
     const uint8_t* qimg;
+    float* lse;                    // optional [batch][q_len][heads] (single-split plans)
     int32_t* err;
 };
 
@@ -921,6 +922,10 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             const float ls = red[n] + red[64 + n] + red[128 + n] + red[192 + n];
             lsum[n] = ls;
             alpha[n] = (n_tiles > 0 && ls > 0.0f) ? p.bmm2_scale / ls : 0.0f;
+            // log-sum-exp of the row's scores: sum_t 2^(x_t) = 2^m l, x in log2 units
+            if (final_out && p.lse && n < rows_here)
+                p.lse[static_cast<int64_t>(b) * p.q_len * p.num_heads + g * kNQ + n] =
+                    (n_tiles > 0 && ls > 0.0f) ? 0.69314718055994531f * (Mrow[n] + log2f(ls)) : -INFINITY;
         }
         named_bar_sync(1, kSoftmaxThreads);
         // O^T -> row-major staging at offset 0 (the ring and Q regions are idle now):
@@ -1065,6 +1070,7 @@ int launch_decode_fp4(const DecodeArgs& a, const DecodePlan& pl, cudaStream_t st
     p.o_sb = a.o_sb; p.o_sq = a.o_sq; p.o_sh = a.o_sh;
     p.part_o = a.part_o; p.part_ml = a.part_ml;
     p.qimg = a.qimg;
+    p.lse = a.lse;
     p.err = a.err;
     const dim3 grid(static_cast<unsigned>(a.batch * pl.groups * pl.splits));
     cudaEvent_t ev0, ev1;

@@ -283,7 +283,30 @@ def mla_decode(query: torch.Tensor, kv_cache: torch.Tensor, workspace_buffer: to
     Returns out [B, q_len, H, kv_lora_rank] bf16.  ``workspace_buffer`` is used for the
     split partials when it is large enough, else a persistent per-device buffer is.
     """
-    del qk_nope_head_dim  # accepted for signature compatibility; MLA absorbed form ignores it
+    del qk_nope_head_dim  # accepted for signature compatibility; the absorbed MLA form ignores it
+    return _decode(query, kv_cache, workspace_buffer, kv_lora_rank, qk_rope_head_dim, block_tables,
+                   seq_lens, max_seq_len, sparse_mla_top_k, out, bmm1_scale, bmm2_scale, None)
+
+
+def mla_decode_lse(query: torch.Tensor, kv_cache: torch.Tensor, workspace_buffer: torch.Tensor | None,
+                   qk_nope_head_dim: int, kv_lora_rank: int, qk_rope_head_dim: int,
+                   block_tables: torch.Tensor, seq_lens: torch.Tensor, max_seq_len: int,
+                   sparse_mla_top_k: int = 0, out: torch.Tensor | None = None,
+                   bmm1_scale: float = 1.0, bmm2_scale: float = 1.0):
+    """mla_decode that also returns lse [B, q_len, H] float32: the natural log of the sum over
+    the visible tokens of exp(bmm1_scale * q.k) (-inf for a row that sees no token).  Results of
+    disjoint token ranges of one sequence merge exactly through it (see ``partition``).
+    Returns (out, lse).  No counterpart in the reference; used by the multi-GPU partition."""
+    del qk_nope_head_dim
+    B, QL, H = query.shape[0], query.shape[1], query.shape[2]
+    lse = torch.empty(B, QL, H, dtype=torch.float32, device=query.device)
+    out = _decode(query, kv_cache, workspace_buffer, kv_lora_rank, qk_rope_head_dim, block_tables,
+                  seq_lens, max_seq_len, sparse_mla_top_k, out, bmm1_scale, bmm2_scale, lse)
+    return out, lse
+
+
+def _decode(query, kv_cache, workspace_buffer, kv_lora_rank, qk_rope_head_dim, block_tables,
+            seq_lens, max_seq_len, sparse_mla_top_k, out, bmm1_scale, bmm2_scale, lse):
     _require_cuda(query, "query")
     _require_cuda(kv_cache, "kv_cache")
     if isinstance(bmm1_scale, torch.Tensor) or isinstance(bmm2_scale, torch.Tensor):
@@ -316,15 +339,17 @@ def mla_decode(query: torch.Tensor, kv_cache: torch.Tensor, workspace_buffer: to
     with _on_device(dev):
         ws_need = mla_decode_workspace_size(B, QL, H, max_seq_len, int(sparse_mla_top_k), dev)
         ws = _workspace(dev, ws_need, workspace_buffer)
-        rc = _lib.lib().nvfp4kv_mla_decode(
-            query.data_ptr(), query.stride(0), query.stride(1), query.stride(2),
-            pool.data_ptr(), pool.shape[0],
-            bt.data_ptr(), bt.stride(0), sl.data_ptr(),
-            B, QL, H, D, kv_lora_rank,
-            int(sparse_mla_top_k), int(page_size), int(max_seq_len),
-            float(bmm1_scale), float(bmm2_scale),
-            out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
-            ws.data_ptr() if ws is not None else None, ws_need,
-            _err_word(dev).data_ptr(), _stream(dev))
+        args = [query.data_ptr(), query.stride(0), query.stride(1), query.stride(2),
+                pool.data_ptr(), pool.shape[0],
+                bt.data_ptr(), bt.stride(0), sl.data_ptr(),
+                B, QL, H, D, kv_lora_rank,
+                int(sparse_mla_top_k), int(page_size), int(max_seq_len),
+                float(bmm1_scale), float(bmm2_scale),
+                out.data_ptr(), out.stride(0), out.stride(1), out.stride(2)]
+        tail = [ws.data_ptr() if ws is not None else None, ws_need, _err_word(dev).data_ptr(), _stream(dev)]
+        if lse is None:
+            rc = _lib.lib().nvfp4kv_mla_decode(*args, *tail)
+        else:
+            rc = _lib.lib().nvfp4kv_mla_decode_lse(*args, lse.data_ptr(), *tail)
     _lib.check(rc, "nvfp4kv_mla_decode")
     return out

@@ -130,6 +130,25 @@ int nvfp4kv_mla_decode(const void* q, int64_t q_stride_b, int64_t q_stride_q, in
                        void* workspace, size_t workspace_bytes,
                        int32_t* err_flag, nvfp4kv_stream_t stream);
 
+/*
+ * nvfp4kv_mla_decode that also writes lse [batch, q_len, num_heads] float32 (contiguous): the
+ * natural-log sum over the visible tokens of exp(bmm1_scale * q.k), -inf for a row with no
+ * visible token.  With it, results over disjoint token ranges of one sequence (computed on
+ * different GPUs) merge exactly: out = sum_r exp(lse_r - lse) out_r, lse = log sum_r exp(lse_r).
+ * No counterpart in the reference (its consumer returns no LSE); used by the multi-GPU
+ * sequence partition.
+ */
+int nvfp4kv_mla_decode_lse(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,
+                           const uint8_t* pool, int64_t pool_rows,
+                           const int32_t* tables, int64_t tables_stride,
+                           const int32_t* seq_lens,
+                           int batch, int q_len, int num_heads, int head_dim_qk, int kv_lora_rank,
+                           int sparse_topk, int page_size, int max_seq_len,
+                           float bmm1_scale, float bmm2_scale,
+                           void* out, int64_t out_stride_b, int64_t out_stride_q, int64_t out_stride_h,
+                           float* lse, void* workspace, size_t workspace_bytes,
+                           int32_t* err_flag, nvfp4kv_stream_t stream);
+
 /* Workspace bytes nvfp4kv_mla_decode needs for this shape on the current device. */
 int nvfp4kv_mla_decode_workspace_size(int batch, int q_len, int num_heads, int max_seq_len,
                                       int sparse_topk, size_t* bytes);
