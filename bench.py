@@ -1,7 +1,8 @@
 #!/usr/bin/env python3
 """Benchmark of the NVFP4 paged KV-cache read path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dense8k|dense128k|sparse|long]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--workload dense8k|dense128k|sparse|long|append]
                     [--impl ours|reference]
 
 Default workload = BASELINE config 2: dense MLA decode over the 288-byte NVFP4 paged pool,
@@ -48,6 +49,11 @@ WORKLOADS = {
                    B=16, H=64, QL=1, ctx=131072, topk=2048),
     # config 4 per layer: 5 x 460,000 + 3 x 900,000 tokens, MTP q_len 3, split over the ranks
     # by the token-balanced sequence partition (strong scaling: the job is fixed)
+    # config 5's append half: 16 x 2048-token chunks per step into a ~2.7M-token pool at random
+    # free pages, latent ~N(0,1) with 1 % of the values at 20x (outliers)
+    "append": dict(desc="config 5 append: 16 seqs x 2048-token chunks per step quantised into a "
+                        "2,713,846-token pool (42,404 pages of 64) at random free pages, 1 % outliers x20",
+                   B=16, H=0, QL=0, ctx=2048, topk=0, pool_tokens=2713846),
     "long": dict(desc="config 4 (one layer): 5 x 460,000 + 3 x 900,000-token sequences, 64 heads, "
                       "MTP q_len 3, token-balanced sequence / page-range partition over the ranks",
                  B=8, H=64, QL=3, ctx=0, topk=0, lens=[460000] * 5 + [900000] * 3),
@@ -182,7 +188,12 @@ def make_layers(rt, torch, wl, layers, dev, seed):
     return out
 
 
+APPEND_BYTES_PER_TOKEN = 1024 + 288 + 8   # bf16 latent read, 288 B row written, int64 slot read
+
+
 def kv_bytes_per_step(wl) -> int:
+    if "pool_tokens" in wl:
+        return wl["B"] * wl["ctx"] * APPEND_BYTES_PER_TOKEN
     if "lens" in wl:
         return sum(wl["lens"]) * NV_BYTES
     rows = wl["B"] * (wl["topk"] if wl["topk"] else wl["ctx"])
@@ -254,6 +265,152 @@ def make_long_step(rt, torch, wl, dev, rank, world, seed):
         state["out"], state["lse"] = P.merge(out_u, lse_u, seq_of, len(lens))
 
     return step, state, sum(u.tokens for u in units) * NV_BYTES
+
+
+def cpu_append_sample(seconds: float):
+    """The oracle's append (C restatement of the reference's _quant_kernel) on 4096 tokens,
+    repeated for ~`seconds`; returns (GB/s of algorithmic bytes, seconds per run, tokens)."""
+    import numpy as np
+    import torch
+
+    from oracle import oracle as O
+
+    T = 4096
+    x = torch.randn(T, 512, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
+    pool = np.zeros((T, NV_BYTES), np.uint8)
+    slots = np.arange(T, dtype=np.int64)
+    runs, t0 = 0, time.perf_counter()
+    while True:
+        O.quant(x, slots, pool)
+        runs += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return runs * T * APPEND_BYTES_PER_TOKEN / el / 1e9, el / runs, T
+
+
+def run_append(args, wl, rt, torch, dist, dev, rank, world, local):
+    """--workload append: quantise-on-append of prefill chunks (weak scaling: a pool per rank)."""
+    T = wl["B"] * wl["ctx"]
+    pages = (wl["pool_tokens"] + 63) // 64
+    pool = torch.zeros(pages, 64, NV_BYTES, dtype=torch.uint8, device=dev)
+    g = torch.Generator().manual_seed(1 + rank)
+    step_bytes = T * APPEND_BYTES_PER_TOKEN
+    n_in = max(2, math.ceil(2 * L2_BYTES / step_bytes))          # inputs read per rotation > 2 x L2
+    inputs = []
+    for k in range(n_in):
+        x = torch.randn(T, 512, generator=g)
+        out_mask = torch.rand(T, 512, generator=g) < 0.01
+        x = torch.where(out_mask, x * 20.0, x).to(torch.bfloat16)
+        # each sequence's 32 new pages go to random free pages of the pool
+        free = torch.randperm(pages, generator=g)[:T // 64]
+        slots = (free.view(-1, 1) * 64 + torch.arange(64).view(1, -1)).reshape(-1).to(torch.int64)
+        inputs.append(dict(x=x.to(dev), slots=slots.to(dev), x_h=x.pin_memory(), slots_h=slots.pin_memory()))
+    for inp in inputs:
+        rt.write_nvfp4(inp["x"], pool, inp["slots"])
+    torch.cuda.synchronize()
+    # one graph holds a whole rotation (n_in appends back to back): a single append is a few
+    # microseconds, shorter than the host's graph-launch interval
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    rot = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(rot, stream=s):
+            for inp in inputs:
+                rt.write_nvfp4(inp["x"], pool, inp["slots"])
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    args.steps = math.ceil(args.steps / n_in) * n_in
+    sampler = ClockSampler(local)
+    sampler.start()
+    soak_end = time.perf_counter() + 1.0
+    k = 0
+    while time.perf_counter() < soak_end or k * n_in < args.warmup:
+        rot.replay()
+        k += 1
+        if k % 64 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for k in range(args.steps // n_in):
+        rot.replay()
+    ev1.record()
+    ev1.synchronize()
+    t1 = time.perf_counter()
+    if world > 1:
+        dist.barrier()
+    sampler.stop()
+    t_max = torch.tensor([ev0.elapsed_time(ev1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms_max = float(t_max.item())
+    per_ms = ms_max / args.steps
+    value = step_bytes * world / (per_ms / 1e3) / 1e9
+
+    # end to end through the public API: the chunk and its slots host->device, the written
+    # rows device->host
+    e_steps = max(10, min(args.e2e_steps, 100))
+    xd, sd = torch.empty_like(inputs[0]["x"]), torch.empty_like(inputs[0]["slots"])
+    rows_h = torch.empty(T, NV_BYTES, dtype=torch.uint8).pin_memory()
+    flat = pool.view(-1, NV_BYTES)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for k in range(e_steps):
+        inp = inputs[k % n_in]
+        xd.copy_(inp["x_h"], non_blocking=True)
+        sd.copy_(inp["slots_h"], non_blocking=True)
+        rt.write_nvfp4(xd, pool, sd)
+        rows_h.copy_(flat.index_select(0, sd), non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = step_bytes * world * e_steps / (float(e_ms.item()) / 1e3) / 1e9
+    errors = rt.device_errors(dev)
+    if rank == 0:
+        peak, peak_kind = load_peaks()
+        achieved = step_bytes / (per_ms / 1e3) / 1e9
+        line = {
+            "metric": "NVFP4 append GB/s (1320 B per token: bf16 latent read, 288 B row and slot)",
+            "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(per_ms, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16->e2m1/e4m3",
+            "data": "synthetic (seeded N(0,1) latent, 1 % of values x20)",
+            "config": {"workload": wl["desc"], "tokens_per_step": T, "pool_pages": pages,
+                       "inputs_rotated": n_in, "steps_per_graph": n_in,
+                       "l2": f"inputs larger than L2: {n_in} chunks x {step_bytes / 2**20:.1f} MiB per rotation",
+                       "parallelism": f"one pool per rank x{world} (weak scaling)"},
+            "tokens_per_s": round(T * world / (per_ms / 1e3), 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                         "per_launch_bytes": step_bytes, "kernel_ms": round(per_ms, 5),
+                         "kernel": "append_kernel", "step_frac_in_kernel": 1.0},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": T * 1024 + T * 8, "d2h_bytes_per_step": T * NV_BYTES,
+                    "steps": e_steps},
+            "gpu_launches": args.steps,
+            "clocks": sampler.summary(t0, t1),
+            "device_errors": errors,
+        }
+        if world == 1:
+            gbs, per, n = cpu_append_sample(args.cpu_seconds)
+            line["cpu_baseline"] = {
+                "value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                "sample": f"oracle append (C restatement of _quant_kernel, one thread) of {n} tokens "
+                          f"repeated for ~{args.cpu_seconds:.0f} s ({per * 1e3:.1f} ms each; {cpu_model()})"}
+        print(json.dumps(line), flush=True)
+    del rot
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_long(args, wl, rt, torch, dist, dev, rank, world, local):
@@ -432,17 +589,27 @@ def reference_arm(args, wl):
     import numpy as np  # noqa: F401
 
     cores = os.cpu_count()
-    cpu_decode_sample(wl, 0.0)                     # warm: build oracle, fault pages in
+    append = "pool_tokens" in wl
+    sample_fn = (lambda: cpu_append_sample(0.0)) if append else (lambda: cpu_decode_sample(wl, 0.0))
+    sample_fn()                                    # warm: build oracle, fault pages in
     times = []
     for i in range(args.warmup + args.steps):
-        gbs, per, ctx = cpu_decode_sample(wl, 0.0)
+        gbs, per, ctx = sample_fn()
         if i >= args.warmup:
             times.append(per)
     per = sum(times) / len(times)
-    value = ctx * NV_BYTES / per / 1e9
-    sample = (f"one sequence of the workload per step ({ctx} tokens x {wl['H']} heads): oracle "
-              f"dequantise (C) + numpy fp32 attention on {cores} host threads ({cpu_model()})")
-    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s",
+    if append:
+        value = ctx * APPEND_BYTES_PER_TOKEN / per / 1e9
+        cores = 1
+        sample = (f"{ctx} tokens per step: oracle append (C restatement of _quant_kernel) on one "
+                  f"host thread ({cpu_model()})")
+    else:
+        value = ctx * NV_BYTES / per / 1e9
+        sample = (f"one sequence of the workload per step ({ctx} tokens x {wl['H']} heads): oracle "
+                  f"dequantise (C) + numpy fp32 attention on {cores} host threads ({cpu_model()})")
+    metric = ("NVFP4 append GB/s (1320 B per token: bf16 latent read, 288 B row and slot)" if append
+              else METRIC)
+    line = {"impl": "reference", "metric": metric, "value": round(value, 4), "unit": "GB/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) latent and q)",
@@ -490,6 +657,9 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     if "lens" in wl:
         run_long(args, wl, rt, torch, dist, dev, rank, world, local)
+        return
+    if "pool_tokens" in wl:
+        run_append(args, wl, rt, torch, dist, dev, rank, world, local)
         return
 
     kvb = kv_bytes_per_step(wl)

@@ -2,8 +2,9 @@
 //
 // Restates _quant_kernel (reference nvfp4-kv/glm53_nvfp4_runtime.py:37-65) for sm_100a:
 // one warp per token, two fully coalesced 16-byte loads per lane (elements [8l, 8l+8) and
-// [256+8l, 256+8l+8)), the block amax completed with one shuffle (a 16-element block spans
-// two neighbouring lanes), and coalesced 4-byte code stores / 1-byte scale stores.
+// [256+8l, 256+8l+8)) issued together with the slot load, the block amax completed with one
+// shuffle (a 16-element block spans two neighbouring lanes), and coalesced 4-byte code
+// stores / 1-byte scale stores.
 //
 // Bit-exactness.  The reference computes v = x / s in fp32 and walks the ladder
 // `|v| < 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5` (ties go up; NaN fails every `<`).  Here the
@@ -24,28 +25,39 @@ __device__ __forceinline__ float to_f32(uint16_t v) {
     else return __half2float(__ushort_as_half(v));
 }
 
-template <int DT, bool VEC>
-__device__ __forceinline__ void load8(const uint16_t* p, float (&x)[8]) {
+// 8 consecutive 16-bit elements, as raw words (converted after every load is in flight).
+template <bool VEC>
+__device__ __forceinline__ uint4 load8_raw(const uint16_t* p) {
     if constexpr (VEC) {
-        uint4 u = *reinterpret_cast<const uint4*>(p);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            x[2 * j] = to_f32<DT>(static_cast<uint16_t>(w[j] & 0xFFFFu));
-            x[2 * j + 1] = to_f32<DT>(static_cast<uint16_t>(w[j] >> 16));
-        }
+        return ldg_nc_v4(p);              // streamed once: no L1 allocation
     } else {
+        uint32_t w[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) x[j] = to_f32<DT>(p[j]);
+        for (int j = 0; j < 4; ++j) w[j] = static_cast<uint32_t>(p[2 * j]) | (static_cast<uint32_t>(p[2 * j + 1]) << 16);
+        return make_uint4(w[0], w[1], w[2], w[3]);
     }
 }
 
-// Code of one element given the block's 7 exact thresholds t_k * s (see file comment).
+template <int DT>
+__device__ __forceinline__ void unpack8(uint4 u, float (&x)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        x[2 * j] = to_f32<DT>(static_cast<uint16_t>(w[j] & 0xFFFFu));
+        x[2 * j + 1] = to_f32<DT>(static_cast<uint16_t>(w[j] >> 16));
+    }
+}
+
+// Code of one element given the block's 7 exact thresholds t_k * s (see file comment): the
+// number of thresholds with !(|x| < t_k s), found by a three-level search over the sorted
+// thresholds (3 compares instead of 7; a NaN fails every `<` and lands on 7 as before).
 __device__ __forceinline__ uint32_t nvfp4_code(float x, const float (&th)[7]) {
     const float a = fabsf(x);
-    uint32_t c = 0;
-#pragma unroll
-    for (int k = 0; k < 7; ++k) c += !(a < th[k]) ? 1u : 0u;
+    const bool b2 = !(a < th[3]);                      // >= 1.75 s: codes 4..7
+    const bool b1 = !(a < (b2 ? th[5] : th[1]));       // >= 3.5 s / 0.75 s
+    const float t0 = b2 ? (b1 ? th[6] : th[4]) : (b1 ? th[2] : th[0]);
+    const bool b0 = !(a < t0);
+    const uint32_t c = (b2 ? 4u : 0u) | (b1 ? 2u : 0u) | (b0 ? 1u : 0u);
     return c | (x < 0.0f ? 8u : 0u);
 }
 
@@ -82,18 +94,22 @@ append_kernel(const uint16_t* __restrict__ src, int64_t T, int64_t stride,
     const int lane = threadIdx.x & 31;
     const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= T) return;
+    // the row and its slot are loaded together (token t's row exists whatever its slot says;
+    // a skipped token's row is simply not stored), so a warp waits one memory latency, not two
+    const uint16_t* row = src + t * stride;
+    const uint4 ua = load8_raw<VEC>(row + 8 * lane);
+    const uint4 ub = load8_raw<VEC>(row + 256 + 8 * lane);
     int64_t sl;
-    if constexpr (SLOT_DT == NVFP4KV_INDEX_I64) sl = static_cast<const int64_t*>(slot)[t];
-    else sl = static_cast<const int32_t*>(slot)[t];
+    if constexpr (SLOT_DT == NVFP4KV_INDEX_I64) sl = __ldg(static_cast<const long long*>(slot) + t);
+    else sl = __ldg(static_cast<const int32_t*>(slot) + t);
     if (sl < 0) return;                                        // runtime:42-43
     if (sl >= pool_rows) {
         if (lane == 0) set_error(err, NVFP4KV_DEVERR_BAD_SLOT);
         return;
     }
-    const uint16_t* row = src + t * stride;
     float xa[8], xb[8];
-    load8<DT, VEC>(row + 8 * lane, xa);
-    load8<DT, VEC>(row + 256 + 8 * lane, xb);
+    unpack8<DT>(ua, xa);
+    unpack8<DT>(ub, xb);
     uint8_t sa, sb;
     const uint32_t ca = quant_half(xa, sa);
     const uint32_t cb = quant_half(xb, sb);
