@@ -928,52 +928,60 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
                     (n_tiles > 0 && ls > 0.0f) ? 0.69314718055994531f * (Mrow[n] + log2f(ls)) : -INFINITY;
         }
         named_bar_sync(1, kSoftmaxThreads);
-        // O^T -> row-major staging at offset 0 (the ring and Q regions are idle now):
-        // warp (sp, hh) moves rows 32hh .. +32 of dims 128 jb + 32 sp + lane.
+        if (final_out) {
+            // O^T -> row-major bf16 staging at offset 0 (the ring and Q regions are idle
+            // now), then one bulk copy per output row (the output has caller strides):
+            // warp (sp, hh) moves rows 32hh .. +32 of dims 128 jb + 32 sp + lane.
 #pragma unroll 1
-        for (int jb = 0; jb < 4; ++jb) {
-            uint32_t o[32];
-            if (n_tiles > 0) {
-                tmem_ld32(tmem + kTO + 64 * jb + 32 * hh + lane_base, o);
-                tmem_wait_ld();
-            } else {
+            for (int jb = 0; jb < 4; ++jb) {
+                uint32_t o[32];
+                if (n_tiles > 0) {
+                    tmem_ld32(tmem + kTO + 64 * jb + 32 * hh + lane_base, o);
+                    tmem_wait_ld();
+                } else {
 #pragma unroll
-                for (int k = 0; k < 32; ++k) o[k] = 0u;
-            }
-            const int d = 128 * jb + t;
-            if (final_out) {
+                    for (int k = 0; k < 32; ++k) o[k] = 0u;
+                }
+                const int d = 128 * jb + t;
                 __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem);
 #pragma unroll
                 for (int k = 0; k < 32; ++k) {
                     const int n = 32 * hh + k;
                     stg[n * kLatent + d] = __float2bfloat16_rn(__uint_as_float(o[k]) * alpha[n]);
                 }
-            } else {
-                float* stg = reinterpret_cast<float*>(smem);
-#pragma unroll
-                for (int k = 0; k < 32; ++k) stg[(32 * hh + k) * kLatent + d] = __uint_as_float(o[k]);
             }
-        }
-        fence_proxy_async_smem();
-        named_bar_sync(1, kSoftmaxThreads);
-        const int n = threadIdx.x;
-        if (n < rows_here) {
-            if (final_out) {
+            fence_proxy_async_smem();
+            named_bar_sync(1, kSoftmaxThreads);
+            const int n = threadIdx.x;
+            if (n < rows_here) {
                 bulk_copy_s2g(p.out + rowoff[n], sbase + n * kLatent * 2, kLatent * 2);
-            } else {
-                const int64_t unit = (static_cast<int64_t>(s) * p.batch + b) * p.groups + g;
-                bulk_copy_s2g(p.part_o + (unit * kNQ + n) * kLatent, sbase + n * kLatent * 4, kLatent * 4);
-                float* ml = p.part_ml + (unit * kNQ + n) * 2;
-                ml[0] = Mrow[n];
-                ml[1] = lsum[n];
+                bulk_commit_group();
+                bulk_wait_group_read0();
             }
-            bulk_commit_group();
-            bulk_wait_group_read0();
-        } else if (!final_out && n < kNQ) {
+        } else {
+            // split partial: unnormalised O rows straight from TMEM to global memory (for one
+            // row k a warp writes 32 consecutive floats), then (max, sum) per row.  A split
+            // that saw no token writes no O values: its sums are 0 and the combine skips it.
             const int64_t unit = (static_cast<int64_t>(s) * p.batch + b) * p.groups + g;
-            float* ml = p.part_ml + (unit * kNQ + n) * 2;
-            ml[0] = -INFINITY;
-            ml[1] = 0.0f;
+            float* po = p.part_o + unit * kNQ * kLatent;
+            if (n_tiles > 0) {
+#pragma unroll 1
+                for (int jb = 0; jb < 4; ++jb) {
+                    uint32_t o[32];
+                    tmem_ld32(tmem + kTO + 64 * jb + 32 * hh + lane_base, o);
+                    tmem_wait_ld();
+                    const int d = 128 * jb + t;
+#pragma unroll
+                    for (int k = 0; k < 32; ++k)
+                        if (32 * hh + k < rows_here) __stcg(po + (32 * hh + k) * kLatent + d, __uint_as_float(o[k]));
+                }
+            }
+            const int n = threadIdx.x;
+            if (n < kNQ) {
+                const bool live = n < rows_here && n_tiles > 0;
+                __stcg(reinterpret_cast<float2*>(p.part_ml + (unit * kNQ + n) * 2),
+                       live ? make_float2(Mrow[n], lsum[n]) : make_float2(-INFINITY, 0.0f));
+            }
         }
     }
 
