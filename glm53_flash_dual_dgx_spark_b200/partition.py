@@ -152,7 +152,8 @@ def merge(parts_out: torch.Tensor, parts_lse: torch.Tensor, seq_of_part: Sequenc
            else torch.as_tensor(list(seq_of_part), dtype=torch.long, device=dev))
     lse = torch.full((batch, QL, H), float("-inf"), dtype=torch.float32, device=dev)
     if P:
-        lse = lse.index_reduce(0, seq, parts_lse.float(), "amax", include_self=True)
+        lse = lse.scatter_reduce(0, seq.view(-1, 1, 1).expand(P, QL, H), parts_lse.float(), "amax",
+                                 include_self=True)
     m = torch.where(torch.isfinite(lse), lse, torch.zeros_like(lse))
     w = torch.exp(parts_lse.float() - m[seq])                     # 0 for a piece with lse -inf
     den = torch.zeros(batch, QL, H, dtype=torch.float32, device=dev).index_add(0, seq, w)
