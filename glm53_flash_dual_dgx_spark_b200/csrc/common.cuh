@@ -183,6 +183,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
+// Programmatic dependent launch: a kernel launched with the programmatic-serialisation
+// attribute may start before the previous kernel of its stream has finished; griddep_wait
+// blocks the calling thread until that kernel has completed and its writes are visible, and
+// griddep_launch_dependents lets the next such kernel start once every block of this one ran it.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Per-warpgroup register budget (setmaxnreg): every thread of the 4 warps of a warpgroup runs
 // the same call.  An increase waits until other warpgroups of the CTA have released enough:
 // the budgets of all warpgroups must add up to no more than the block was launched with.

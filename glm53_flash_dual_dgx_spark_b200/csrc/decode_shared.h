@@ -45,6 +45,24 @@ struct DecodeArgs {
     int32_t* err;
 };
 
+// Launch `kernel` as a programmatic dependent of the kernel before it on `st`: it may start
+// while that kernel still runs, and reads that kernel's output only after griddepcontrol.wait.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                             Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Q preparation + the fused decode kernel (QK^T on the block-scaled fp4 tensor-core path),
 // paged (sparse_topk == 0) or top-k rows (sparse_topk > 0).
 int launch_decode_fp4(const DecodeArgs& a, const DecodePlan& pl, cudaStream_t st);

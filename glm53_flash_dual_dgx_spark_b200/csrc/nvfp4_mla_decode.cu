@@ -33,6 +33,7 @@ combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_
                __nv_bfloat16* __restrict__ out, int64_t o_sb, int64_t o_sq, int64_t o_sh,
                float* __restrict__ lse) {
     __shared__ float wts[kMaxSplits];
+    griddep_wait();   // a programmatic dependent of the attention kernel that writes the partials
     const int n = blockIdx.x % kNQ;
     const int bg = blockIdx.x / kNQ;
     const int g = bg % groups, b = bg / groups;
@@ -233,10 +234,12 @@ int decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q
         if ((rc = launch_decode_fp4(a, pl, st)) != NVFP4KV_OK) return rc;
     }
     if (pl.splits > 1) {
-        combine_kernel<<<batch * pl.groups * kNQ, 128, 0, st>>>(part_o, part_ml, pl.splits, batch, pl.groups,
-                                                          q_len, num_heads, bmm2_scale,
-                                                          static_cast<__nv_bfloat16*>(out), out_stride_b,
-                                                          out_stride_q, out_stride_h, lse);
+        const cudaError_t le = launch_dependent(
+            combine_kernel, dim3(batch * pl.groups * kNQ), dim3(128), 0, st, part_o, part_ml, pl.splits, batch,
+            pl.groups, q_len, num_heads, bmm2_scale, static_cast<__nv_bfloat16*>(out), out_stride_b, out_stride_q,
+            out_stride_h, lse);
+        if (le != cudaSuccess)
+            return fail(NVFP4KV_ECUDA, "nvfp4kv_mla_decode combine launch failed: %s", cudaGetErrorString(le));
         if ((rc = check_launch("nvfp4kv_mla_decode combine")) != NVFP4KV_OK) return rc;
     }
     return NVFP4KV_OK;

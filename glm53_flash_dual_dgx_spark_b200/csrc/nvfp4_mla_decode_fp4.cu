@@ -149,6 +149,7 @@ struct QPrepParams {
 // first term's scales stay within e4m3; each later term codes the residual of the earlier
 // ones.  One warp per row, one lane per 16-dim block; grid = groups x 8 blocks of 8 rows.
 __global__ void __launch_bounds__(256) q_prep_kernel(const QPrepParams p) {
+    griddep_launch_dependents();   // the attention kernel may start its set-up meanwhile
     const int unit = blockIdx.x >> 3;
     const int b = unit / p.groups, g = unit % p.groups;
     const int lane = threadIdx.x & 31;
@@ -506,13 +507,16 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = static_cast<uint32_t>(flags[0]);
+    griddep_launch_dependents();   // the split combine may be scheduled; it waits for this grid
 
     if (warp >= kMmaWarp) {
     warpgroup_reg_dealloc<kRegsCtl>();
     if (warp == kTmaWarp) {
         // ============================================================ TMA / bulk loads
         if (lane == 0) {
-            // (a kernel-boundary dependency: the Q preparation kernel ran before this launch)
+            // the Q image is the output of the Q preparation kernel this one may overlap (all
+            // else this kernel reads was complete before that kernel started)
+            griddep_wait();
             const uint8_t* img = p.qimg + static_cast<size_t>(b * p.groups + g) * kQImageBytes;
             mbar_arrive_expect_tx(bar(B_Q), static_cast<uint32_t>(kQImageBytes));
             bulk_copy_g2s(sbase + SM_QB, img, 2 * kCodeBytes, bar(B_Q));
@@ -1084,10 +1088,13 @@ int launch_decode_fp4(const DecodeArgs& a, const DecodePlan& pl, cudaStream_t st
     cudaEvent_t ev0, ev1;
     take_kernel_events(&ev0, &ev1);
     if (ev0 && cudaEventRecord(ev0, st) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaEventRecord failed");
-    if (sparse)
-        decode_fp4_kernel<true><<<grid, kThreads, kSmemBytes, st>>>(p, tm_codes, tm_scales);
-    else
-        decode_fp4_kernel<false><<<grid, kThreads, kSmemBytes, st>>>(p, tm_codes, tm_scales);
+    // a programmatic dependent of the Q preparation: set-up overlaps that kernel's tail
+    const cudaError_t le =
+        sparse ? launch_dependent(decode_fp4_kernel<true>, grid, dim3(kThreads), kSmemBytes, st, p, tm_codes, tm_scales)
+               : launch_dependent(decode_fp4_kernel<false>, grid, dim3(kThreads), kSmemBytes, st, p, tm_codes,
+                                  tm_scales);
+    if (le != cudaSuccess)
+        return fail(NVFP4KV_ECUDA, "nvfp4kv_mla_decode: attention launch failed: %s", cudaGetErrorString(le));
     if ((rc = check_launch(sparse ? "nvfp4kv_mla_decode (fp4 sparse)" : "nvfp4kv_mla_decode (fp4 dense)")) != NVFP4KV_OK)
         return rc;
     if (ev1 && cudaEventRecord(ev1, st) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaEventRecord failed");
