@@ -13,6 +13,18 @@
 // t*s without being equal to it, so fl(x/s) < t  <=>  |x| < t*s.  s == 0 makes every
 // threshold 0 and every code 7, like x/0 = +-inf and 0/0 = NaN in the reference; the sign
 // nibble is (x < 0), which equals (x/s < 0) for every s >= 0 and a bf16/fp16 x.
+//
+// Fast path.  The ladder is round-to-nearest onto the e2m1 grid {0, 0.5, 1, 1.5, 2, 3, 4, 6}
+// with ties rounded up (each threshold is the midpoint of two neighbours) and everything
+// from 5 up mapped to 6.  So the code of x is the hardware conversion
+// cvt.rn.satfinite.e2m1x2.f32 of v = x * r, where r = RN(RN(1/s) * (1 + 2^-18)):
+// v / (x/s) lies in (1, 1 + 2^-17), which moves an exact tie x = t*s strictly above t (so
+// it rounds up, not to even), while a bf16/fp16 x != t*s is at least 2^-11 (relative) away
+// from t*s (t*s has at most 7 significant bits and is itself a bf16/fp16 value), so it stays
+// on its side.  v is formed as fma(x, r, +0.0) so that x = -0.0 gives +0.0 (code 0, as in
+// the reference), while a negative x that rounds to zero keeps its sign (code 8).  A block
+// whose scale byte is 0 (x/0) or whose elements include a NaN takes the exact compare
+// ladder below instead, for its whole warp.
 #include "abi_common.h"
 #include "common.cuh"
 
@@ -86,6 +98,42 @@ __device__ __forceinline__ uint32_t quant_half(const float (&x)[8], uint8_t& sca
     return packed;
 }
 
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+__device__ __forceinline__ float abs_max_nan8(const float (&x)[8]) {
+    float m = fabsf(x[0]);
+#pragma unroll
+    for (int j = 1; j < 8; ++j) m = max_nan(m, fabsf(x[j]));
+    return m;
+}
+
+// Fast-path codes of 8 consecutive elements: cvt.rn.satfinite.e2m1x2 of fma(x, r, +0.0)
+// (see the file comment), packed with element 0 in the low nibble of byte 0.
+__device__ __forceinline__ uint32_t e2m1x8_scaled(const float (&x)[8], float r) {
+    uint32_t packed;
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+        ".reg .f32 v0, v1, v2, v3, v4, v5, v6, v7;\n\t"
+        "fma.rn.f32 v0, %1, %9, 0f00000000;\n\t"
+        "fma.rn.f32 v1, %2, %9, 0f00000000;\n\t"
+        "fma.rn.f32 v2, %3, %9, 0f00000000;\n\t"
+        "fma.rn.f32 v3, %4, %9, 0f00000000;\n\t"
+        "fma.rn.f32 v4, %5, %9, 0f00000000;\n\t"
+        "fma.rn.f32 v5, %6, %9, 0f00000000;\n\t"
+        "fma.rn.f32 v6, %7, %9, 0f00000000;\n\t"
+        "fma.rn.f32 v7, %8, %9, 0f00000000;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b0, v1, v0;\n\t"   // first source -> high nibble
+        "cvt.rn.satfinite.e2m1x2.f32 b1, v3, v2;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b2, v5, v4;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b3, v7, v6;\n\t"
+        "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+        : "=r"(packed)
+        : "f"(x[0]), "f"(x[1]), "f"(x[2]), "f"(x[3]), "f"(x[4]), "f"(x[5]), "f"(x[6]), "f"(x[7]), "f"(r));
+    return packed;
+}
+
 template <int DT, int SLOT_DT, bool VEC>
 __global__ void __launch_bounds__(256)
 append_kernel(const uint16_t* __restrict__ src, int64_t T, int64_t stride,
@@ -110,15 +158,31 @@ append_kernel(const uint16_t* __restrict__ src, int64_t T, int64_t stride,
     float xa[8], xb[8];
     unpack8<DT>(ua, xa);
     unpack8<DT>(ub, xb);
-    uint8_t sa, sb;
-    const uint32_t ca = quant_half(xa, sa);
-    const uint32_t cb = quant_half(xb, sb);
     uint8_t* dst = pool + sl * kRowBytes;
-    *reinterpret_cast<uint32_t*>(dst + 4 * lane) = ca;         // bytes [4l, 4l+4)
-    *reinterpret_cast<uint32_t*>(dst + 128 + 4 * lane) = cb;   // bytes [128+4l, ...)
-    if ((lane & 1) == 0) {
-        dst[256 + (lane >> 1)] = sa;                           // block l/2
-        dst[256 + 16 + (lane >> 1)] = sb;                      // block 16 + l/2
+    // block amax, NaN-propagating: a NaN anywhere in the block sends the warp to the ladder
+    float ma = abs_max_nan8(xa), mb = abs_max_nan8(xb);
+    ma = max_nan(ma, __shfl_xor_sync(0xFFFFFFFFu, ma, 1));
+    mb = max_nan(mb, __shfl_xor_sync(0xFFFFFFFFu, mb, 1));
+    // the two lanes of a pair share blocks l/2 (half a) and 16 + l/2 (half b): the even lane
+    // computes the first one's scale, the odd lane the second one's
+    const bool odd = lane & 1;
+    const float m = odd ? mb : ma;
+    const uint8_t sbyte = f32_to_e4m3(fmaxf(__fdiv_rn(m, 6.0f), 1e-8f));   // runtime:47-48
+    const float s = e4m3_to_f32(sbyte);                                   // runtime:49
+    // r > 0 only on the fast path (s > 0 and no NaN); 1 + 2^-18 is exact in fp32
+    const float r = (s > 0.0f && m == m) ? __fmul_rn(__frcp_rn(s), 1.0000038146972656f) : 0.0f;
+    if (__all_sync(0xFFFFFFFFu, r > 0.0f)) {
+        const float r_other = __shfl_xor_sync(0xFFFFFFFFu, r, 1);
+        dst[256 + 16 * odd + (lane >> 1)] = sbyte;             // block l/2 or 16 + l/2
+        *reinterpret_cast<uint32_t*>(dst + 4 * lane) = e2m1x8_scaled(xa, odd ? r_other : r);
+        *reinterpret_cast<uint32_t*>(dst + 128 + 4 * lane) = e2m1x8_scaled(xb, odd ? r : r_other);
+    } else {
+        uint8_t sa, sb;
+        const uint32_t ca = quant_half(xa, sa);
+        const uint32_t cb = quant_half(xb, sb);
+        *reinterpret_cast<uint32_t*>(dst + 4 * lane) = ca;         // bytes [4l, 4l+4)
+        *reinterpret_cast<uint32_t*>(dst + 128 + 4 * lane) = cb;   // bytes [128+4l, ...)
+        dst[256 + 16 * odd + (lane >> 1)] = odd ? sb : sa;          // NaN-ignoring amax here
     }
 }
 
