@@ -134,8 +134,11 @@ __device__ __forceinline__ uint32_t e2m1x8_scaled(const float (&x)[8], float r) 
     return packed;
 }
 
+// At most 32 registers a thread, so that 8 blocks (64 warps, 64 tokens in flight) fit on an
+// SM: the latency of the row loads is covered by occupancy (two or four tokens per warp, at
+// fewer warps an SM, measured slower).
 template <int DT, int SLOT_DT, bool VEC>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 8)
 append_kernel(const uint16_t* __restrict__ src, int64_t T, int64_t stride,
               uint8_t* __restrict__ pool, int64_t pool_rows, const void* __restrict__ slot,
               int32_t* __restrict__ err) {
