@@ -183,6 +183,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
+// 16-byte asynchronous copy global -> shared (L2 only), `src_bytes` (0 or 16) read from
+// `src` and the rest zero-filled; both addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst_smem, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst_smem), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+// The calling thread's earlier cp.async copies arrive on `bar` once they have landed (the
+// barrier's pending count is raised first, so this adds no expected arrival).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 // Programmatic dependent launch: a kernel launched with the programmatic-serialisation
 // attribute may start before the previous kernel of its stream has finished; griddep_wait
 // blocks the calling thread until that kernel has completed and its writes are visible, and

@@ -16,13 +16,12 @@
 //
 // Work unit (one CTA): query group (b, g) of up to 64 rows (MTP token i, head h) x token split.
 // Warps: 0-7 softmax (warp w: TMEM sub-partition w & 3 = tokens of the tile, query rows
-// 32 (w >> 2) .. +32), 8 MMA issue, 9-12 producers, 13 loads.  Per 128-token tile i:
-//   loads    ring of tiles: codes [2 x 128 rows x 128 B] swizzled + scales [128 x 32 B].
-//            Dense (paged): 3 slots filled by TMA boxes straight from the pages; pages missing
-//            or beyond the context load as out-of-range boxes (zeros).  Sparse (top-k rows):
-//            2 slots; the warp bulk-copies the 128 rows (288 B each) into a staging buffer in
-//            the third slot's space and rearranges them into the ring layout, zeros for
-//            masked rows, so everything downstream is shared with the dense path.
+// 32 (w >> 2) .. +32), 8-11 producers, 12 MMA issue, 13 loads.  Per 128-token tile i:
+//   loads    3-slot ring of tiles: codes [2 x 128 rows x 128 B] swizzled + scales [128 x 32 B].
+//            Dense (paged): TMA boxes straight from the pages; pages missing or beyond the
+//            context load as out-of-range boxes (zeros).  Sparse (top-k rows): each lane
+//            copies its rows with 16-byte asynchronous copies straight into the slot layout,
+//            zero-filling masked rows, so everything downstream is shared with the dense path.
 //   producers  V chunks of 16 tokens -> fp16 [8 d-atoms x 16 tokens x 128 B] (2 buffers).
 //   MMA      QK(i): 16 fp4 MMAs M128 N128 K64 -> S^T; PV(i-1): 8 chunks x 4 fp16 MMAs.
 //   softmax  S^T row t -> x = s * log2(e) * bmm1_scale, masked; the running max of each query
@@ -48,7 +47,7 @@ constexpr int kTile = kDecTile;                   // 128 tokens: QK M
 constexpr int kNQ = kDecRows;                     // 64 query rows: PV N
 constexpr int kChunk = 16;                        // tokens per V chunk = PV K
 constexpr int kChunks = kTile / kChunk;           // 8
-constexpr int kSlots = 3;                         // tile ring depth (dense; sparse uses 2 + staging)
+constexpr int kSlots = 3;                         // tile ring depth
 constexpr int kVBufs = 2;                         // V chunk buffers
 // Four warpgroups.  Registers are moved between them at run time (setmaxnreg): the block is
 // launched with 128 per thread; softmax takes 168, producers keep 96, the control group 80.
@@ -84,7 +83,7 @@ constexpr int SM_FLAGS = SM_ROWOFF + 64 * 8;              // [0] TMEM base, [1] 
 constexpr int SM_TMASK = SM_FLAGS + 16;                   // kSlots x 4 words: tile rows that are valid
 constexpr int SM_BARS = SM_TMASK + kSlots * 16;
 enum {
-    B_FULL = 0,                    // [kSlots] raw tile landed (TMA transaction bytes)
+    B_FULL = 0,                    // [kSlots] raw tile landed (TMA bytes / cp.async arrivals)
     B_FREE = B_FULL + kSlots,      // [kSlots] producers finished reading the slot
     B_QKD = B_FREE + kSlots,       // [kSlots] QK finished reading the slot
     B_SFA_FULL = B_QKD + kSlots,   // [2] pool scales of a tile written to TMEM
@@ -95,7 +94,6 @@ enum {
     B_V_FULL,                      // [kVBufs] V chunk written
     B_V_EMPTY = B_V_FULL + kVBufs, // [kVBufs] PV finished reading the V chunk
     B_Q = B_V_EMPTY + kVBufs,      // prepared Q landed (set-up)
-    B_STAGE,                       // sparse: rows of the next tile landed in the staging buffer
     B_DRAIN,                       // every MMA of the CTA complete (before TMEM is freed)
     kNumBars
 };
@@ -286,51 +284,41 @@ __device__ __forceinline__ int64_t token_row(const Fp4Params& p, const int* sidx
     }
 }
 
-// Sparse: bulk-copy the rows of tile `tile_start` (288 B each, lane l copies rows l + 32k)
-// into the staging buffer at `stage`, row r at r * 288.  Masked rows are not copied; the
-// transaction count covers exactly the rows that are.  Returns bit k set when row l + 32k was.
-__device__ __forceinline__ uint32_t load_rows(const Fp4Params& p, uint32_t stage, uint32_t bar_stage,
-                                              const int* sidx, bool staged, int idx_base, int b,
-                                              int tile_start, int end, int lane) {
-    int64_t rows[4];
+// Sparse: the rows of tile `tile_start` (lane l: rows l + 32k) straight into the ring slot at
+// `slot_base` with 16-byte asynchronous copies: codes into the 128-byte swizzled K-major
+// atoms, scales at 32 B per row.  Masked rows (-1 padding, out-of-range entries, positions
+// past `end`) are zero-filled without a read.  Every lane's copies arrive on `bar_full`
+// once landed; lane 0 then writes the slot's valid-row mask and makes the barrier's one
+// expected arrival, so the phase completes when the mask is written and every row is in.
+__device__ __forceinline__ void load_rows_async(const Fp4Params& p, uint32_t slot_base, uint32_t bar_full,
+                                                uint32_t* slot_mask, const int* sidx, bool staged,
+                                                int idx_base, int b, int tile_start, int end, int lane) {
     uint32_t live = 0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        const int pos = tile_start + 32 * k + lane;
-        rows[k] = pos < end ? token_row<true>(p, sidx, staged, idx_base, b, pos, true) : -1;
-        live |= static_cast<uint32_t>(rows[k] >= 0) << k;
-    }
-    int n = __popc(live);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) n += __shfl_xor_sync(0xFFFFFFFFu, n, off);
-    if (lane == 0) mbar_arrive_expect_tx(bar_stage, static_cast<uint32_t>(n) * kRowBytes);
-    __syncwarp();
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-        if (rows[k] >= 0)
-            bulk_copy_g2s(stage + (32 * k + lane) * kRowBytes, p.pool + rows[k] * kRowBytes, kRowBytes,
-                          bar_stage);
-    return live;
-}
-
-// Sparse: staged rows -> ring slot layout (codes in 128-byte swizzled K-major atoms, scales
-// at 32 B per row); rows whose bit in `live` is clear become zeros.  Lane l moves rows l + 32k.
-__device__ __forceinline__ void rows_to_slot(const uint8_t* stage, uint8_t* slot, uint32_t live, int lane) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
         const int r = 32 * k + lane;
-        const bool ok = (live >> k) & 1u;
-        const uint4* src = reinterpret_cast<const uint4*>(stage + r * kRowBytes);
-        uint8_t* dst = slot + (r >> 3) * 1024 + (r & 7) * 128;
+        const int pos = tile_start + r;
+        const int64_t row = pos < end ? token_row<true>(p, sidx, staged, idx_base, b, pos, true) : -1;
+        const bool ok = row >= 0;
+        live |= static_cast<uint32_t>(ok) << k;
+        const uint8_t* src = p.pool + (ok ? row : 0) * kRowBytes;
+        const uint32_t nbytes = ok ? 16u : 0u;
+        const uint32_t drow = slot_base + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-            const uint4 v = ok ? src[c] : make_uint4(0u, 0u, 0u, 0u);
-            *reinterpret_cast<uint4*>(dst + (c >> 3) * 16384 + (((c & 7) ^ (r & 7)) << 4)) = v;
-        }
+        for (int c = 0; c < 16; ++c)
+            cp_async16_zfill(drow + (c >> 3) * 16384 + (((c & 7) ^ (r & 7)) << 4), src + 16 * c, nbytes);
 #pragma unroll
         for (int h = 0; h < 2; ++h)
-            reinterpret_cast<uint4*>(slot + kCodeBytes + r * 32)[h] = ok ? src[16 + h] : make_uint4(0u, 0u, 0u, 0u);
+            cp_async16_zfill(slot_base + kCodeBytes + r * 32 + 16 * h, src + 256 + 16 * h, nbytes);
     }
+    cp_async_mbar_arrive(bar_full);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t w = __ballot_sync(0xFFFFFFFFu, (live >> k) & 1u);
+        if (lane == 0) slot_mask[k] = w;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar_full);
 }
 
 // Pool scales of the tile in `slot` -> TMEM scale-factor columns `col` of this warp's
@@ -432,9 +420,6 @@ template <bool kSparse>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ CUtensorMap tm_codes,
                   const __grid_constant__ CUtensorMap tm_scales) {
-    constexpr int kRing = kSparse ? 2 : kSlots;
-    constexpr int SM_STAGING = SM_STAGE + 2 * kSlotBytes;   // sparse: 128 raw rows of 288 B
-    static_assert(kTile * kRowBytes <= kSlotBytes, "staging buffer fits a ring slot");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -487,7 +472,6 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
         mbar_init(bar(B_P_FULL), kSoftmaxWarps);
         mbar_init(bar(B_PV_DONE), 1);
         mbar_init(bar(B_Q), 1);
-        mbar_init(bar(B_STAGE), 1);
         mbar_init(bar(B_DRAIN), 1);
         flags[1] = 0;
         mbar_fence_init();
@@ -528,41 +512,28 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             }
         }
         if constexpr (kSparse) {
-            // tile j: rows -> staging -> slot j & 1 once QK(j-2) and the producers are done with it
-            uint32_t live = 0;
-            int issued = 0;   // staging loads issued; load k completes phase k of B_STAGE
-            if (n_tiles > 0) {
-                live = load_rows(p, sbase + SM_STAGING, bar(B_STAGE), sidx, staged, idx_base, b, start, end, lane);
-                issued = 1;
+            // tile j -> slot j % kSlots once QK(j - kSlots) and the producers are done with it
+            int issued = 0;   // tiles issued; tile j completes phase j / kSlots of its slot
+            for (int j = 0; j < kSlots && j < n_tiles; ++j) {
+                load_rows_async(p, sbase + SM_STAGE + j * kSlotBytes, bar(B_FULL + j), tmask + 4 * j, sidx,
+                                staged, idx_base, b, start + j * kTile, end, lane);
+                issued = j + 1;
             }
 #pragma unroll 1
-            for (int j = 0; j < n_tiles; ++j) {
-                const int slot = j & 1;
-                bool ok = mbar_wait(bar(B_STAGE), j & 1, abort_flag, p.err);
-                if (j >= 2) {
-                    ok &= mbar_wait(bar(B_FREE + slot), ((j - 2) >> 1) & 1, abort_flag, p.err);
-                    ok &= mbar_wait(bar(B_QKD + slot), ((j - 2) >> 1) & 1, abort_flag, p.err);
-                }
+            for (int i = 0; i + kSlots < n_tiles; ++i) {
+                const int slot = i % kSlots;
+                const uint32_t sph = (i / kSlots) & 1;
+                const bool f = mbar_wait(bar(B_FREE + slot), sph, abort_flag, p.err);
+                const bool d = mbar_wait(bar(B_QKD + slot), sph, abort_flag, p.err);
                 // after an abort nothing more is issued (the drain below waits for what was)
-                if (!__all_sync(0xFFFFFFFFu, ok && !*abort_flag)) break;
-                rows_to_slot(smem + SM_STAGING, smem + SM_STAGE + slot * kSlotBytes, live, lane);
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const uint32_t w = __ballot_sync(0xFFFFFFFFu, (live >> k) & 1u);
-                    if (lane == 0) tmask[4 * slot + k] = w;
-                }
-                // the slot is read by the tensor core; the staging buffer is refilled by bulk copies
+                if (!__all_sync(0xFFFFFFFFu, f && d && !*abort_flag)) break;
                 fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar(B_FULL + slot));
-                if (j + 1 < n_tiles) {
-                    live = load_rows(p, sbase + SM_STAGING, bar(B_STAGE), sidx, staged, idx_base, b,
-                                     start + (j + 1) * kTile, end, lane);
-                    issued = j + 2;
-                }
+                load_rows_async(p, sbase + SM_STAGE + slot * kSlotBytes, bar(B_FULL + slot), tmask + 4 * slot,
+                                sidx, staged, idx_base, b, start + (i + kSlots) * kTile, end, lane);
+                issued = i + kSlots + 1;
             }
-            // drain: at most the last staging load can still be landing
-            if (issued > 0) mbar_drain_wait(bar(B_STAGE), (issued - 1) & 1);
+            for (int j = issued > kSlots ? issued - kSlots : 0; j < issued; ++j)
+                mbar_drain_wait(bar(B_FULL + j % kSlots), (j / kSlots) & 1);
         } else if (lane == 0) {
             int issued = 0;   // tiles loaded; tile j completes phase j / kSlots of slot j % kSlots
             for (int j = 0; j < kSlots && j < n_tiles; ++j) {
@@ -600,11 +571,12 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
 #pragma unroll 1
         for (int i = 0; i <= n_tiles; ++i) {
             if (i < n_tiles) {
-                const int slot = i % kRing, fb = i & 1;
-                mbar_wait(bar(B_FULL + slot), (i / kRing) & 1, abort_flag, p.err);
+                const int slot = i % kSlots, fb = i & 1;
+                mbar_wait(bar(B_FULL + slot), (i / kSlots) & 1, abort_flag, p.err);
                 mbar_wait(bar(B_SFA_FULL + fb), (i >> 1) & 1, abort_flag, p.err);
                 if (i > 0) mbar_wait(bar(B_S_FREE), (i - 1) & 1, abort_flag, p.err);
                 tc_fence_after();
+                if constexpr (kSparse) fence_proxy_async_smem();   // cp.async rows -> tensor core
                 const uint64_t da0 = smem_desc_sw128(sbase + SM_STAGE + slot * kSlotBytes, 16, 1024);
                 const uint32_t sfa = tmem + kTSFA + 32 * fb, sfb = tmem + kTSFB;
                 if (elect_one()) {
@@ -652,36 +624,16 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
         warpgroup_reg_dealloc<kRegsProducer>();
         // ============================================================ producers: V chunks
         // lane -> token tq = lane & 15 of the chunk; 16-byte code chunks (32 dims) sc0 =
-        // 4 pw + (lane >> 4) and sc0 + 2.  Sparse: warp pw also writes the pool scales of each
-        // tile (A scale factors) into its TMEM sub-partition pw, one tile ahead of QK (dense
-        // tiles land early, so the softmax warps do it there, off the V-chunk chain).
+        // 4 pw + (lane >> 4) and sc0 + 2.
         const int pw = warp - kProducerWarp0;
-        const uint32_t lane_base = static_cast<uint32_t>(32 * pw) << 16;
-        // scales of tile j -> TMEM slot j & 1.  Its last reader, QK(j-2), is complete: the
-        // producers reach tile j-1 only after PV(j-2) chunk 5, which the tensor core runs
-        // after QK(j-1).
-        auto write_sfa = [&](int j) {
-            const int sl = j % kRing;
-            mbar_wait(bar(B_FULL + sl), (j / kRing) & 1, abort_flag, p.err);
-            tc_fence_after();
-            scales_to_tmem(smem + SM_STAGE + sl * kSlotBytes + kCodeBytes, tmem + kTSFA + 32 * (j & 1) + lane_base, lane);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(B_SFA_FULL + (j & 1)));
-        };
-        // a sparse tile is rearranged into its slot only once the slot's previous tile is
-        // done: give that two chunks of time before the next tile's scales are written
-        constexpr int kSfaChunk = 2;
-        if (kSparse && n_tiles > 0) write_sfa(0);
 #pragma unroll 1
         for (int i = 0; i < n_tiles; ++i) {
-            const int slot = i % kRing;
-            mbar_wait(bar(B_FULL + slot), (i / kRing) & 1, abort_flag, p.err);
+            const int slot = i % kSlots;
+            mbar_wait(bar(B_FULL + slot), (i / kSlots) & 1, abort_flag, p.err);
             const uint8_t* codes = smem + SM_STAGE + slot * kSlotBytes;
             const uint8_t* scales = codes + kCodeBytes;
 #pragma unroll 1
             for (int c = 0; c < kChunks; ++c) {
-                if (kSparse && c == kSfaChunk && i + 1 < n_tiles) write_sfa(i + 1);
                 const int u = kChunks * i + c, vb = u % kVBufs;
                 const int tq = lane & 15;
                 const int tok = c * kChunk + tq;
@@ -762,7 +714,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             tmem_st32(tmem + kTSFB + 32 * hh + lane_base, rr);
             tmem_wait_st();
         }
-        if (!kSparse && hh == 0 && n_tiles > 0) {
+        if (hh == 0 && n_tiles > 0) {
             mbar_wait(bar(B_FULL + 0), 0, abort_flag, p.err);
             scales_to_tmem(smem + SM_STAGE + kCodeBytes, tmem + kTSFA + lane_base, lane);
             tc_fence_before();
@@ -778,11 +730,11 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
         for (int i = 0; i < n_tiles; ++i) {
             mbar_wait(bar(B_S_FULL), i & 1, abort_flag, p.err);
             tc_fence_after();
-            // dense: pool scales of tile i+1 -> its TMEM slot (QK(i-1), the slot's last reader,
-            // is complete: S_FULL(i) tracks every earlier MMA)
-            if (!kSparse && hh == 0 && i + 1 < n_tiles) {
-                const int slot1 = (i + 1) % kRing;
-                mbar_wait(bar(B_FULL + slot1), ((i + 1) / kRing) & 1, abort_flag, p.err);
+            // pool scales of tile i+1 -> its TMEM slot (QK(i-1), the slot's last reader, is
+            // complete: S_FULL(i) tracks every earlier MMA); the ring loads tiles two ahead
+            if (hh == 0 && i + 1 < n_tiles) {
+                const int slot1 = (i + 1) % kSlots;
+                mbar_wait(bar(B_FULL + slot1), ((i + 1) / kSlots) & 1, abort_flag, p.err);
                 scales_to_tmem(smem + SM_STAGE + slot1 * kSlotBytes + kCodeBytes,
                                tmem + kTSFA + 32 * ((i + 1) & 1) + lane_base, lane);
                 tc_fence_before();
@@ -805,8 +757,8 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             const int pos = start + i * kTile + t;
             // valid row of the tile: the load warp publishes the mask with the slot's barrier
             // (complete long before S^T of the tile exists, and not re-armed before P(i))
-            mbar_wait(bar(B_FULL + i % kRing), (i / kRing) & 1, abort_flag, p.err);
-            const bool tok_ok = (tmask[4 * (i % kRing) + (t >> 5)] >> (t & 31)) & 1u;
+            mbar_wait(bar(B_FULL + i % kSlots), (i / kSlots) & 1, abort_flag, p.err);
+            const bool tok_ok = (tmask[4 * (i % kSlots) + (t >> 5)] >> (t & 31)) & 1u;
             // Probabilities against the running row maxima, computed speculatively in place:
             // p = 2^(s qs - m).  They stand unless some visible score exceeds its row's max by
             // more than 2^8 (a vote over the CTA); then the maxima move and p is recomputed.
