@@ -68,9 +68,9 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic(workload: str):
-    """Per-launch DRAM bytes of the decode kernel from a committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", f"mla_decode_{workload}.md")
+def profile_traffic(workload: str, summary: str = ""):
+    """Per-launch DRAM bytes of the workload's kernel from a committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", summary or f"mla_decode_{workload}.md")
     if not os.path.exists(p):
         return None
     for line in open(p):
@@ -390,7 +390,8 @@ def run_append(args, wl, rt, torch, dist, dev, rank, world, local):
                        "parallelism": f"one pool per rank x{world} (weak scaling)"},
             "tokens_per_s": round(T * world / (per_ms / 1e3), 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": profile_traffic("append", "append_config5.md"),
                          "per_launch_bytes": step_bytes, "kernel_ms": round(per_ms, 5),
                          "kernel": "append_kernel", "step_frac_in_kernel": 1.0},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
