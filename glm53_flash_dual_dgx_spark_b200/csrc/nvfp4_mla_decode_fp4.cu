@@ -145,23 +145,10 @@ struct QPrepParams {
 // swizzle); its per-16 e4m3 scales to [pass][row][32]; qs[n] = log2e * bmm1_scale * 2^e_n.
 // Each row is first scaled by 2^-e_n (exact) so its largest |q| lies in [2^10, 2^11) and the
 // first term's scales stay within e4m3; each later term codes the residual of the earlier
-// ones.  One warp per row, one lane per 16-dim block; grid = groups x 8 blocks of 8 rows.
-__global__ void __launch_bounds__(256) q_prep_kernel(const QPrepParams p) {
-    griddep_launch_dependents();   // the attention kernel may start its set-up meanwhile
-    const int unit = blockIdx.x >> 3;
-    const int b = unit / p.groups, g = unit % p.groups;
-    const int lane = threadIdx.x & 31;
-    const int n = ((blockIdx.x & 7) << 3) | (threadIdx.x >> 5);
-    const int rows_here = min(kNQ, p.q_len * p.num_heads - g * kNQ);
-    const bool real = n < rows_here;
-    const int r = g * kNQ + n;
-    const int qi = real ? r / p.num_heads : 0, h = real ? r % p.num_heads : 0;
-    uint4 u0 = make_uint4(0, 0, 0, 0), u1 = make_uint4(0, 0, 0, 0);
-    if (real) {
-        const __nv_bfloat16* src = p.q + b * p.q_sb + qi * p.q_sq + h * p.q_sh + 16 * lane;
-        u0 = ldg_nc_v4(src);
-        u1 = ldg_nc_v4(src + 8);
-    }
+// ones.  One warp per row, one lane per 16-dim block: q_prep_row quantises row n of the
+// group from its 16 bf16 values per lane (u0, u1; zeros for rows past the group).
+__device__ __forceinline__ void q_prep_row(const QPrepParams& p, int unit, int n, bool real, int lane,
+                                           uint4 u0, uint4 u1) {
     const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
     float x[16];
     float amax = 0.0f;
@@ -206,6 +193,25 @@ __global__ void __launch_bounds__(256) q_prep_kernel(const QPrepParams p) {
     }
     if (lane == 0)
         reinterpret_cast<float*>(img + 2 * kCodeBytes + 2 * 4096)[n] = real ? p.scale_log2 * ldexpf(1.0f, e) : 0.0f;
+}
+
+// grid = groups x 8 blocks of 8 rows (one warp per row).
+__global__ void __launch_bounds__(256) q_prep_kernel(const QPrepParams p) {
+    griddep_launch_dependents();   // the attention kernel may start its set-up meanwhile
+    const int unit = blockIdx.x >> 3;
+    const int b = unit / p.groups, g = unit % p.groups;
+    const int lane = threadIdx.x & 31;
+    const int n = ((blockIdx.x & 7) << 3) | (threadIdx.x >> 5);
+    const int rows_here = min(kNQ, p.q_len * p.num_heads - g * kNQ);
+    const bool real = n < rows_here;
+    uint4 u0 = make_uint4(0, 0, 0, 0), u1 = make_uint4(0, 0, 0, 0);
+    if (real) {
+        const int r = g * kNQ + n, qi = r / p.num_heads, h = r % p.num_heads;
+        const __nv_bfloat16* src = p.q + b * p.q_sb + qi * p.q_sq + h * p.q_sh + 16 * lane;
+        u0 = ldg_nc_v4(src);
+        u1 = ldg_nc_v4(src + 8);
+    }
+    q_prep_row(p, unit, n, real, lane, u0, u1);
 }
 
 __device__ __forceinline__ int page_id(const Fp4Params& p, const int* sidx, bool staged, int idx_base,
@@ -497,19 +503,21 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
     warpgroup_reg_dealloc<kRegsCtl>();
     if (warp == kTmaWarp) {
         // ============================================================ TMA / bulk loads
-        if (lane == 0) {
-            // the Q image is the output of the Q preparation kernel this one may overlap (all
-            // else this kernel reads was complete before that kernel started)
+        // The Q image is the output of the Q preparation kernel this one may overlap (all else
+        // this kernel reads was complete before that kernel started).  Sparse: it is copied
+        // right after the first tile's row gather, which does not depend on it and takes the
+        // longer; dense: first (measured: the dense step lost 0.2 us the other way round).
+        auto load_q = [&]() {
             griddep_wait();
             const uint8_t* img = p.qimg + static_cast<size_t>(b * p.groups + g) * kQImageBytes;
             mbar_arrive_expect_tx(bar(B_Q), static_cast<uint32_t>(kQImageBytes));
             bulk_copy_g2s(sbase + SM_QB, img, 2 * kCodeBytes, bar(B_Q));
             bulk_copy_g2s(sbase + SM_PT, img + 2 * kCodeBytes, 2 * 4096, bar(B_Q));
             bulk_copy_g2s(sbase + SM_QS, img + 2 * kCodeBytes + 2 * 4096, 256, bar(B_Q));
-            if constexpr (!kSparse) {
-                tma_prefetch_desc(&tm_codes);
-                tma_prefetch_desc(&tm_scales);
-            }
+        };
+        if (!kSparse && lane == 0) {
+            tma_prefetch_desc(&tm_codes);
+            tma_prefetch_desc(&tm_scales);
         }
         if constexpr (kSparse) {
             // tile j -> slot j % kSlots once QK(j - kSlots) and the producers are done with it
@@ -518,7 +526,9 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
                 load_rows_async(p, sbase + SM_STAGE + j * kSlotBytes, bar(B_FULL + j), tmask + 4 * j, sidx,
                                 staged, idx_base, b, start + j * kTile, end, lane);
                 issued = j + 1;
+                if (j == 0 && lane == 0) load_q();
             }
+            if (n_tiles == 0 && lane == 0) load_q();
 #pragma unroll 1
             for (int i = 0; i + kSlots < n_tiles; ++i) {
                 const int slot = i % kSlots;
@@ -535,6 +545,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             for (int j = issued > kSlots ? issued - kSlots : 0; j < issued; ++j)
                 mbar_drain_wait(bar(B_FULL + j % kSlots), (j / kSlots) & 1);
         } else if (lane == 0) {
+            load_q();
             int issued = 0;   // tiles loaded; tile j completes phase j / kSlots of slot j % kSlots
             for (int j = 0; j < kSlots && j < n_tiles; ++j) {
                 load_tile(p, &tm_codes, &tm_scales, sbase, bar(B_FULL + j), sidx, staged, idx_base, b,
