@@ -16,6 +16,7 @@ LIB_PATH = os.environ.get("NVFP4KV_LIB", os.path.join(HERE, "libnvfp4kv.so"))
 # Return and device-error codes (include/nvfp4kv.h).
 OK, EINVAL, EWORKSPACE, ECUDA = 0, 1, 2, 3
 DEVERR_TIMEOUT, DEVERR_BAD_SLOT, DEVERR_BAD_INDEX, DEVERR_BAD_PAGE, DEVERR_SEQ_LEN = 1, 2, 4, 8, 16
+DEVERR_CAPACITY = 32
 DTYPE_BF16, DTYPE_F16 = 0, 1
 INDEX_I64, INDEX_I32 = 0, 1
 
@@ -27,6 +28,8 @@ SIGNATURES = {
     "nvfp4kv_append": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, _I, _P, _P]),
     "nvfp4kv_gather_ds656": (_I, [_P, _I64, _P, _I64, _P, _P]),
     "nvfp4kv_dequant_bf16": (_I, [_P, _I64, _P, _I, _I64, _P, _P, _P]),
+    "nvfp4kv_dedup_gather_ds656": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I64, _P, _P, _P]),
+    "nvfp4kv_dedup_workspace_ints": (_I, [_I64, _I64, ctypes.POINTER(_I64)]),
     "nvfp4kv_mla_decode": (_I, [_P, _I64, _I64, _I64,          # q + strides
                                 _P, _I64,                      # pool, pool_rows
                                 _P, _I64,                      # tables, tables_stride

@@ -33,14 +33,9 @@ __device__ __forceinline__ void decode_block(uint2 codes, uint8_t scale_byte, fl
     }
 }
 
-// runtime:87-122.  Row r of `out` re-encodes pool row clamp(idx[r], 0, R-1).
-__global__ void __launch_bounds__(256)
-gather_ds656_kernel(const uint8_t* __restrict__ pool, int64_t R, const int32_t* __restrict__ idx,
-                    int64_t S, uint8_t* __restrict__ out) {
-    const int lane = threadIdx.x & 31;
-    const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (r >= S) return;
-    int64_t src = idx[r];
+// runtime:87-122.  One warp: the 656-byte row at `dst` re-encodes pool row clamp(src, 0, R-1).
+__device__ __forceinline__ void gather_row_ds656(const uint8_t* __restrict__ pool, int64_t R, int64_t src,
+                                                 uint8_t* __restrict__ dst, int lane) {
     src = src < 0 ? 0 : (src > R - 1 ? R - 1 : src);          // :98
     const uint8_t* row = pool + src * kRowBytes;
     const uint2 codes = ldg_nc_v2(row + 8 * lane);
@@ -64,10 +59,168 @@ gather_ds656_kernel(const uint8_t* __restrict__ pool, int64_t R, const int32_t* 
             w |= static_cast<uint32_t>(f32_to_e4m3(__fmul_rn(v[4 * j + k], inv))) << (8 * k);
         o[j] = w;
     }
-    uint8_t* dst = out + r * kDsBytes;
     *reinterpret_cast<uint4*>(dst + 16 * lane) = make_uint4(o[0], o[1], o[2], o[3]);  // :117-120
     if ((lane & 7) == 0) *reinterpret_cast<float*>(dst + 512 + 4 * (lane >> 3)) = gscale;  // :114
     *reinterpret_cast<uint32_t*>(dst + 528 + 4 * lane) = 0u;                           // :121-122
+}
+
+// Row r of `out` re-encodes pool row clamp(idx[r], 0, R-1).
+__global__ void __launch_bounds__(256)
+gather_ds656_kernel(const uint8_t* __restrict__ pool, int64_t R, const int32_t* __restrict__ idx,
+                    int64_t S, uint8_t* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= S) return;
+    gather_row_ds656(pool, R, idx[r], out + r * kDsBytes, lane);
+}
+
+// ------------------------------------------------------------------ sync-free dedup
+// The distinct values of the block tables, ascending, as torch.unique sorts them
+// (runtime:177-182): a mark per possible value (key 0 = -1, key r + 1 = pool row r), an
+// exclusive scan of the marks giving each value its position, the inverse tables read off
+// the scan, and the gather driven by the device-side count.  Fixed grids: no host sync.
+constexpr int kScanBlock = 1024;
+constexpr int kScanPerThread = 4;
+constexpr int kScanTile = kScanBlock * kScanPerThread;   // marks per scan block
+
+__device__ __forceinline__ int64_t dedup_key(int32_t e, int64_t R, int32_t* err) {
+    if (e == -1) return 0;
+    if (e < 0 || e >= R) {   // counted as -1; the reference would keep it as its own value
+        set_error(err, NVFP4KV_DEVERR_BAD_INDEX);
+        return 0;
+    }
+    return static_cast<int64_t>(e) + 1;
+}
+
+__global__ void __launch_bounds__(256)
+dedup_mark_kernel(const int32_t* __restrict__ entries, int64_t n, int64_t R, int32_t* __restrict__ marks,
+                  int32_t* __restrict__ err) {
+    const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j < n) marks[dedup_key(entries[j], R, err)] = 1;
+}
+
+// Block-wide exclusive scan of one value per thread; returns this thread's prefix and sets
+// `total` (every thread) to the block's sum.
+__device__ __forceinline__ int32_t block_exclusive_scan(int32_t v, int32_t& total) {
+    __shared__ int32_t warp_sums[kScanBlock / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int32_t x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int32_t y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int32_t w = warp_sums[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int32_t y = __shfl_up_sync(0xFFFFFFFFu, w, o);
+            if (lane >= o) w += y;
+        }
+        warp_sums[lane] = w;   // inclusive over warps
+    }
+    __syncthreads();
+    total = warp_sums[kScanBlock / 32 - 1];
+    const int32_t before = warp == 0 ? 0 : warp_sums[warp - 1];
+    __syncthreads();           // warp_sums is reused by the next call
+    return before + x - v;
+}
+
+__global__ void __launch_bounds__(kScanBlock)
+dedup_block_sums_kernel(const int32_t* __restrict__ marks, int64_t M, int32_t* __restrict__ bsum) {
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanTile + kScanPerThread * threadIdx.x;
+    int32_t s = 0;
+#pragma unroll
+    for (int k = 0; k < kScanPerThread; ++k)
+        if (base + k < M) s += marks[base + k];
+    int32_t total;
+    block_exclusive_scan(s, total);
+    if (threadIdx.x == 0) bsum[blockIdx.x] = total;
+}
+
+// One block: exclusive scan of the nb block sums in place, in chunks of kScanBlock with a
+// running carry; the grand total is the number of distinct entries.
+__global__ void __launch_bounds__(kScanBlock)
+dedup_scan_sums_kernel(int32_t* __restrict__ bsum, int64_t nb, int32_t* __restrict__ n_unique) {
+    int32_t carry = 0;
+    for (int64_t c = 0; c < nb; c += kScanBlock) {
+        const int64_t i = c + threadIdx.x;
+        const int32_t v = i < nb ? bsum[i] : 0;
+        int32_t total;
+        const int32_t ex = block_exclusive_scan(v, total);
+        if (i < nb) bsum[i] = carry + ex;
+        carry += total;
+    }
+    if (threadIdx.x == 0) *n_unique = carry;
+}
+
+// Marks -> positions (in place), and the ascending list of distinct values.
+__global__ void __launch_bounds__(kScanBlock)
+dedup_offsets_kernel(int32_t* __restrict__ marks, int64_t M, const int32_t* __restrict__ bsum,
+                     int32_t* __restrict__ uniq) {
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanTile + kScanPerThread * threadIdx.x;
+    int32_t m[kScanPerThread];
+    int32_t s = 0;
+#pragma unroll
+    for (int k = 0; k < kScanPerThread; ++k) {
+        m[k] = base + k < M ? marks[base + k] : 0;
+        s += m[k];
+    }
+    int32_t total;
+    int32_t pos = bsum[blockIdx.x] + block_exclusive_scan(s, total);
+#pragma unroll
+    for (int k = 0; k < kScanPerThread; ++k) {
+        if (base + k < M) {
+            marks[base + k] = pos;
+            if (m[k]) uniq[pos] = static_cast<int32_t>(base + k - 1);   // key 0 -> -1
+        }
+        pos += m[k];
+    }
+}
+
+__global__ void __launch_bounds__(256)
+dedup_tables_kernel(const int32_t* __restrict__ entries, int64_t n, int64_t R, const int32_t* __restrict__ pos,
+                    int32_t* __restrict__ tables) {
+    const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j < n) tables[j] = pos[dedup_key(entries[j], R, nullptr)];
+}
+
+// Warp u (grid-stride) writes scratch row u: the gathered row of distinct value u for
+// u < n_unique, zeros up to the next multiple of 64 rows, within `cap` rows.
+__global__ void __launch_bounds__(256)
+dedup_gather_kernel(const uint8_t* __restrict__ pool, int64_t R, const int32_t* __restrict__ uniq,
+                    const int32_t* __restrict__ n_unique, uint8_t* __restrict__ scratch, int64_t cap,
+                    int32_t* __restrict__ err) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nu = *n_unique;
+    const int64_t padded = (nu + 63) / 64 * 64;
+    const int64_t end = padded < cap ? padded : cap;
+    if (blockIdx.x == 0 && threadIdx.x == 0 && nu > cap) set_error(err, NVFP4KV_DEVERR_CAPACITY);
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t u = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); u < end;
+         u += warps) {
+        uint8_t* dst = scratch + u * kDsBytes;
+        if (u < nu) {
+            gather_row_ds656(pool, R, uniq[u], dst, lane);
+        } else {
+            reinterpret_cast<uint4*>(dst)[lane] = make_uint4(0u, 0u, 0u, 0u);   // 512 B
+            if (lane < 9) reinterpret_cast<uint4*>(dst + 512)[lane] = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
+}
+
+struct DedupLayout {
+    int64_t M, nb, uniq_len, ints;   // marks [M], block sums [nb], uniq [uniq_len]
+};
+DedupLayout dedup_layout(int64_t pool_rows, int64_t n) {
+    DedupLayout l{};
+    l.M = pool_rows + 1;
+    l.nb = (l.M + kScanTile - 1) / kScanTile;
+    l.uniq_len = n < l.M ? n : l.M;
+    l.ints = l.M + l.nb + l.uniq_len;
+    return l;
 }
 
 template <int IDT>
@@ -137,4 +290,62 @@ extern "C" int nvfp4kv_dequant_bf16(const uint8_t* pool, int64_t pool_rows, cons
     else
         return fail(NVFP4KV_EINVAL, "nvfp4kv_dequant_bf16: rows dtype must be int64 or int32");
     return check_launch("nvfp4kv_dequant_bf16");
+}
+
+extern "C" int nvfp4kv_dedup_workspace_ints(int64_t pool_rows, int64_t num_entries, int64_t* ints) {
+    using namespace nvfp4kv;
+    if (!ints) return fail(NVFP4KV_EINVAL, "nvfp4kv_dedup_workspace_ints: null output");
+    if (pool_rows <= 0 || num_entries < 0 || pool_rows >= (int64_t(1) << 31) - 1)
+        return fail(NVFP4KV_EINVAL, "nvfp4kv_dedup_workspace_ints: bad pool_rows / num_entries");
+    *ints = dedup_layout(pool_rows, num_entries).ints;
+    return NVFP4KV_OK;
+}
+
+extern "C" int nvfp4kv_dedup_gather_ds656(const uint8_t* pool, int64_t pool_rows, const int32_t* entries,
+                                          int64_t num_entries, int32_t* workspace, int64_t workspace_ints,
+                                          int32_t* tables, uint8_t* scratch, int64_t scratch_rows,
+                                          int32_t* n_unique, int32_t* err_flag, nvfp4kv_stream_t stream) {
+    using namespace nvfp4kv;
+    if (num_entries < 0 || scratch_rows < 0)
+        return fail(NVFP4KV_EINVAL, "nvfp4kv_dedup_gather_ds656: negative size");
+    if (!pool || !workspace || !n_unique || (num_entries > 0 && (!entries || !tables)) ||
+        (scratch_rows > 0 && !scratch))
+        return fail(NVFP4KV_EINVAL, "nvfp4kv_dedup_gather_ds656: null pointer");
+    if (pool_rows <= 0 || pool_rows >= (int64_t(1) << 31) - 1)
+        return fail(NVFP4KV_EINVAL, "nvfp4kv_dedup_gather_ds656: bad pool_rows");
+    if (reinterpret_cast<uintptr_t>(pool) % 16 || reinterpret_cast<uintptr_t>(scratch) % 16)
+        return fail(NVFP4KV_EINVAL, "nvfp4kv_dedup_gather_ds656: pool and scratch must be 16-byte aligned");
+    const DedupLayout l = dedup_layout(pool_rows, num_entries);
+    if (workspace_ints < l.ints)
+        return fail(NVFP4KV_EWORKSPACE, "nvfp4kv_dedup_gather_ds656: workspace %lld ints < %lld",
+                    (long long)workspace_ints, (long long)l.ints);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int32_t* marks = workspace;
+    int32_t* bsum = workspace + l.M;
+    int32_t* uniq = bsum + l.nb;
+    cudaError_t e = cudaMemsetAsync(marks, 0, static_cast<size_t>(l.M) * sizeof(int32_t), st);
+    if (e != cudaSuccess) return fail(NVFP4KV_ECUDA, "nvfp4kv_dedup_gather_ds656: memset: %s", cudaGetErrorString(e));
+    int rc;
+    const unsigned eb = static_cast<unsigned>((num_entries + 255) / 256);
+    if (num_entries > 0) {
+        dedup_mark_kernel<<<eb, 256, 0, st>>>(entries, num_entries, pool_rows, marks, err_flag);
+        if ((rc = check_launch("nvfp4kv_dedup_gather_ds656 (mark)")) != NVFP4KV_OK) return rc;
+    }
+    dedup_block_sums_kernel<<<static_cast<unsigned>(l.nb), kScanBlock, 0, st>>>(marks, l.M, bsum);
+    if ((rc = check_launch("nvfp4kv_dedup_gather_ds656 (block sums)")) != NVFP4KV_OK) return rc;
+    dedup_scan_sums_kernel<<<1, kScanBlock, 0, st>>>(bsum, l.nb, n_unique);
+    if ((rc = check_launch("nvfp4kv_dedup_gather_ds656 (scan)")) != NVFP4KV_OK) return rc;
+    dedup_offsets_kernel<<<static_cast<unsigned>(l.nb), kScanBlock, 0, st>>>(marks, l.M, bsum, uniq);
+    if ((rc = check_launch("nvfp4kv_dedup_gather_ds656 (positions)")) != NVFP4KV_OK) return rc;
+    if (num_entries > 0) {
+        dedup_tables_kernel<<<eb, 256, 0, st>>>(entries, num_entries, pool_rows, marks, tables);
+        if ((rc = check_launch("nvfp4kv_dedup_gather_ds656 (tables)")) != NVFP4KV_OK) return rc;
+    }
+    if (scratch_rows > 0) {
+        const int64_t want = (scratch_rows + 7) / 8;   // 8 warps a block, one row each per pass
+        const unsigned grid = static_cast<unsigned>(want < 148 * 16 ? want : 148 * 16);
+        dedup_gather_kernel<<<grid, 256, 0, st>>>(pool, pool_rows, uniq, n_unique, scratch, scratch_rows, err_flag);
+        if ((rc = check_launch("nvfp4kv_dedup_gather_ds656 (gather)")) != NVFP4KV_OK) return rc;
+    }
+    return NVFP4KV_OK;
 }

@@ -191,6 +191,54 @@ def build_scratch(kv_cache: torch.Tensor, block_tables: torch.Tensor):
     return scratch, inv.to(torch.int32).view(T, 1, K)
 
 
+def build_scratch_sync_free(kv_cache: torch.Tensor, block_tables: torch.Tensor,
+                            capacity_rows: int | None = None):
+    """The T > _SYNC_FREE_T branch of build_scratch without a host synchronisation.
+
+    The reference deduplicates with torch.unique (runtime:177-182), which synchronises to
+    size its output.  Here the distinct entries are found, numbered in ascending order and
+    gathered on the device by fixed-size launches (nvfp4kv_dedup_gather_ds656), so the call
+    is asynchronous and CUDA-graph capturable.  Returns (scratch [P_cap, 64, 656] uint8,
+    tables [T, 1, K] int32, n_unique int32 [1] on the device).  tables equals the
+    reference's; the reference's scratch is the first ceil(n_unique / 64) pages of this one
+    (rows from n_unique to the end of that page are zero); later pages are not written.
+    P_cap covers capacity_rows rows, by default min(T * K, pool rows + 1), the most distinct
+    entries there can be; fewer rows than the distinct entries set NVFP4KV_DEVERR_CAPACITY.
+    """
+    pool = kv_cache.view(-1, NV_BYTES)
+    _require_cuda(pool, "kv_cache")
+    _require_cuda(block_tables, "block_tables")
+    if block_tables.dim() != 3:
+        raise ValueError("block_tables must be [T, 1, K]")
+    if block_tables.dtype != torch.int32:
+        raise TypeError("block_tables must be int32")
+    T, one, K = block_tables.shape
+    flat = block_tables.reshape(-1).contiguous()
+    n = flat.numel()
+    R = pool.shape[0]
+    cap = min(n, R + 1) if capacity_rows is None else int(capacity_rows)
+    if cap < 0:
+        raise ValueError("capacity_rows must be >= 0")
+    dev = pool.device
+    P = (cap + 63) // 64
+    scratch = torch.empty(P, 64, DS_BYTES, dtype=torch.uint8, device=dev)
+    tables = torch.empty(n, dtype=torch.int32, device=dev)
+    n_unique = torch.empty(1, dtype=torch.int32, device=dev)
+    ints = ctypes.c_int64()
+    _lib.check(_lib.lib().nvfp4kv_dedup_workspace_ints(R, n, ctypes.byref(ints)), "nvfp4kv_dedup_workspace_ints")
+    key = ("dedup", dev.index)
+    ws = _bufs.get(key)
+    if ws is None or ws.numel() < ints.value:
+        ws = torch.empty(ints.value, dtype=torch.int32, device=dev)
+        _bufs[key] = ws
+    with _on_device(dev):
+        rc = _lib.lib().nvfp4kv_dedup_gather_ds656(pool.data_ptr(), R, flat.data_ptr(), n, ws.data_ptr(),
+                                                   ws.numel(), tables.data_ptr(), scratch.data_ptr(), P * 64,
+                                                   n_unique.data_ptr(), _err_word(dev).data_ptr(), _stream(dev))
+    _lib.check(rc, "nvfp4kv_dedup_gather_ds656")
+    return scratch, tables.view(T, 1, K), n_unique
+
+
 def dequant(kv_cache: torch.Tensor, rows: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """Pool rows -> bf16 [n, 512] (exact); rows outside the pool (and -1) read as zeros."""
     pool = kv_cache.view(-1, NV_BYTES)

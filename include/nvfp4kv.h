@@ -44,6 +44,7 @@ extern "C" {
 #define NVFP4KV_DEVERR_BAD_INDEX 4  /* sparse index < -1 or >= pool_rows (masked) */
 #define NVFP4KV_DEVERR_BAD_PAGE 8   /* page id < 0 or >= num_pages (masked) */
 #define NVFP4KV_DEVERR_SEQ_LEN 16   /* seq_len beyond the table / top-k width (clamped) */
+#define NVFP4KV_DEVERR_CAPACITY 32  /* more distinct rows than the scratch holds (truncated) */
 
 /* input element types */
 #define NVFP4KV_DTYPE_BF16 0
@@ -85,6 +86,33 @@ int nvfp4kv_append(const void* kv_c, int kv_dtype, int64_t num_tokens, int64_t s
  */
 int nvfp4kv_gather_ds656(const uint8_t* pool, int64_t pool_rows, const int32_t* idx,
                          int64_t num_rows, uint8_t* out, nvfp4kv_stream_t stream);
+
+/*
+ * Sync-free deduplicating gather: the T > _SYNC_FREE_T branch of build_scratch
+ * (nvfp4-kv/glm53_nvfp4_runtime.py:177-182: torch.unique(flat, return_inverse=True) then
+ * _gather into a zeroed [ceil(S/64), 64, 656] scratch) without the host synchronisation
+ * torch.unique needs for its data-dependent size.  All outputs are written on the device, in
+ * stream order, by fixed-size launches (CUDA-graph capturable):
+ *   tables[j]  = position of entries[j] among the distinct entries in ascending order (the
+ *                inverse of torch.unique), int32;
+ *   scratch    = row u (656 B) is the _gather_kernel row of distinct entry u (-1 reads row 0)
+ *                for u < *n_unique, and zeros up to the next multiple of 64 rows;
+ *   *n_unique  = number of distinct entries (device int32).
+ * entries: num_entries int32 pool rows, -1 padded.  Entries < -1 or >= pool_rows set
+ * NVFP4KV_DEVERR_BAD_INDEX and count as -1 (the reference keeps each such value distinct and
+ * gathers its clamped row).  scratch holds scratch_rows rows (16-byte aligned); with more
+ * distinct entries than that, the first scratch_rows rows are written and
+ * NVFP4KV_DEVERR_CAPACITY is set.  workspace: nvfp4kv_dedup_workspace_ints() int32 values,
+ * no initial contents needed.  pool_rows < 2^31 - 1.
+ */
+int nvfp4kv_dedup_gather_ds656(const uint8_t* pool, int64_t pool_rows, const int32_t* entries,
+                               int64_t num_entries, int32_t* workspace, int64_t workspace_ints,
+                               int32_t* tables, uint8_t* scratch, int64_t scratch_rows,
+                               int32_t* n_unique, int32_t* err_flag, nvfp4kv_stream_t stream);
+
+/* int32 workspace size of nvfp4kv_dedup_gather_ds656 (pool_rows + 1 marks, one value per
+ * 4096 marks, min(num_entries, pool_rows + 1) distinct values). */
+int nvfp4kv_dedup_workspace_ints(int64_t pool_rows, int64_t num_entries, int64_t* ints);
 
 /*
  * Dequantise pool rows to bf16: out[r, :] = decode(pool[rows[r]]) for 0 <= rows[r] <

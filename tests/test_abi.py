@@ -21,7 +21,7 @@ def declared_functions():
 def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     names = declared_functions()
-    assert len(names) == 12, names
+    assert len(names) == 14, names
     for n in names:
         assert hasattr(lib, n), n
     assert set(names) == set(_lib.SIGNATURES)
@@ -71,6 +71,28 @@ def test_gather_and_decode_argument_checks_without_launch():
     assert call(rows=1000) == _lib.EINVAL          # not a multiple of the page size
     assert call(sh=577) == _lib.EINVAL             # q stride not a multiple of 8
     assert call(ws=None, wsb=0) == _lib.EWORKSPACE  # 2 sequences x 1024 tokens need splits
+    assert b"workspace" in lib.nvfp4kv_last_error()
+
+
+def test_dedup_workspace_and_argument_checks_without_launch():
+    lib = _lib.lib()
+    ints = ctypes.c_int64()
+    # 4096 pool rows: 4097 marks, one block sum per 4096 marks, min(entries, 4097) values
+    assert lib.nvfp4kv_dedup_workspace_ints(4096, 19200, ctypes.byref(ints)) == _lib.OK
+    assert ints.value == 4097 + 2 + 4097
+    assert lib.nvfp4kv_dedup_workspace_ints(4096, 100, ctypes.byref(ints)) == _lib.OK
+    assert ints.value == 4097 + 2 + 100
+    assert lib.nvfp4kv_dedup_workspace_ints(0, 100, ctypes.byref(ints)) == _lib.EINVAL
+    assert lib.nvfp4kv_dedup_workspace_ints(4096, -1, ctypes.byref(ints)) == _lib.EINVAL
+    assert lib.nvfp4kv_dedup_workspace_ints(4096, 1, None) == _lib.EINVAL
+    call = lib.nvfp4kv_dedup_gather_ds656
+    # (pool, rows, entries, n, ws, ws_ints, tables, scratch, scratch_rows, n_unique, err, stream)
+    assert call(None, 4096, 64, 10, 64, 8300, 64, 64, 64, 64, None, None) == _lib.EINVAL    # null pool
+    assert call(4096, 4096, 64, -1, 64, 8300, 64, 64, 64, 64, None, None) == _lib.EINVAL    # n < 0
+    assert call(4096, 4096, 64, 10, 64, 8300, 64, None, 64, 64, None, None) == _lib.EINVAL  # no scratch
+    assert call(4096, 4096, 64, 10, 64, 8300, 64, 4100, 64, 64, None, None) == _lib.EINVAL  # unaligned
+    assert call(4096, 0, 64, 10, 64, 8300, 64, 64, 64, 64, None, None) == _lib.EINVAL       # empty pool
+    assert call(4096, 4096, 64, 10, 64, 100, 64, 64, 64, 64, None, None) == _lib.EWORKSPACE
     assert b"workspace" in lib.nvfp4kv_last_error()
 
 
