@@ -16,7 +16,9 @@ value  = KV bytes read (288 B per attended token row) per second, whole job (all
          device-timed with CUDA events over exactly K steps replayed from CUDA graphs.
 e2e    = the same metric through the public API (glm53_nvfp4_runtime.mla_decode), eager,
          with the per-step q / page-table / seq_lens host->device copies and the output
-         device->host copy (pinned buffers) inside the timed region.
+         device->host copy (pinned buffers) inside the timed region; the copies of the next
+         and previous steps overlap the decode (copy streams, double buffers), as in a
+         serving loop; the one-stream serial figure is reported as e2e.serial_value.
 Multi-GPU (torchrun): each rank owns its own 16 sequences and their pages (weak scaling);
 NCCL is used after the timed loop only, to gather the outputs and the max time.
 """
@@ -727,39 +729,76 @@ def main() -> None:
     value = kvb * args.steps * world / sec / 1e9
     tokens_s = wl["B"] * wl["QL"] * args.steps * world / sec
 
-    # ---- end to end through the public API (eager, host buffers, copies in the region)
+    # ---- end to end through the public API (eager, host buffers, copies in the region).
+    # Pipelined as a serving loop runs it: step k+1's q / tables / seq_lens go host->device on
+    # a copy stream while step k decodes, and step k's output comes back on a third stream;
+    # two buffer sets, with events ordering every reuse.  Every step's copies are inside the
+    # timed region.  The serial variant (one stream: copies, decode, read-back) is reported
+    # beside it.
     e2e_steps = max(args.e2e_steps, 10)
-    q_h = [ly["q_h"] for ly in L]
-    out_h = torch.empty(wl["B"], wl["QL"], wl["H"], 512, dtype=torch.bfloat16).pin_memory()
     h2d = L[0]["q_h"].numel() * 2 + L[0]["tables_h"].numel() * 4 + L[0]["seq_h"].numel() * 4
-    d2h = out_h.numel() * 2
-    qd = torch.empty_like(L[0]["q"])
-    td = torch.empty_like(L[0]["tables"])
-    sd = torch.empty_like(L[0]["seq"])
-    od = torch.empty_like(L[0]["out"])
-    for k in range(3):
+    d2h = L[0]["out"].numel() * 2
+
+    def e2e_run(pipelined: bool) -> float:
+        nb = 2 if pipelined else 1
+        ins = [(torch.empty_like(L[0]["q"]), torch.empty_like(L[0]["tables"]), torch.empty_like(L[0]["seq"]))
+               for _ in range(nb)]
+        outs = [torch.empty_like(L[0]["out"]) for _ in range(nb)]
+        outs_h = [torch.empty(L[0]["out"].shape, dtype=torch.bfloat16).pin_memory() for _ in range(nb)]
+        main = torch.cuda.current_stream()
+        cin = torch.cuda.Stream() if pipelined else main
+        cout = torch.cuda.Stream() if pipelined else main
+        ev = lambda: torch.cuda.Event()   # noqa: E731
+        in_ready = [ev() for _ in range(e2e_steps)]
+        dec_done = [ev() for _ in range(e2e_steps)]
+        out_done = [ev() for _ in range(e2e_steps)]
+
+        def h2d_copy(k):
+            ly, bset = L[k % layers], ins[k % nb]
+            with torch.cuda.stream(cin):
+                if k >= nb:
+                    cin.wait_event(dec_done[k - nb])          # decode k - nb has read this set
+                bset[0].copy_(ly["q_h"], non_blocking=True)
+                bset[1].copy_(ly["tables_h"], non_blocking=True)
+                bset[2].copy_(ly["seq_h"], non_blocking=True)
+                in_ready[k].record(cin)
+
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cin)
+        h2d_copy(0)
+        for k in range(e2e_steps):
+            if pipelined and k + 1 < e2e_steps:
+                h2d_copy(k + 1)
+            elif not pipelined and k > 0:
+                h2d_copy(k)
+            b = k % nb
+            main.wait_event(in_ready[k])
+            if k >= nb:
+                main.wait_event(out_done[k - nb])             # the output set was read back
+            qd, td, sd = ins[b]
+            rt.mla_decode(qd, L[k % layers]["pool"], None, 128, 512, 64, td, sd, wl["topk"] or wl["ctx"],
+                          sparse_mla_top_k=wl["topk"], out=outs[b], bmm1_scale=sm, bmm2_scale=1.0)
+            dec_done[k].record(main)
+            with torch.cuda.stream(cout):
+                cout.wait_event(dec_done[k])
+                outs_h[b].copy_(outs[b], non_blocking=True)
+                out_done[k].record(cout)
+        e1.record(cout)
+        e1.synchronize()
+        torch.cuda.synchronize()
+        e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        return kvb * e2e_steps * world / (float(e_ms.item()) / 1e3) / 1e9
+
+    for k in range(3):                             # warm the eager path
         ly = L[k % layers]
-        qd.copy_(q_h[k % layers], non_blocking=True)
-        call(dict(ly, q=qd), out=od)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for k in range(e2e_steps):
-        ly = L[k % layers]
-        qd.copy_(ly["q_h"], non_blocking=True)
-        td.copy_(ly["tables_h"], non_blocking=True)
-        sd.copy_(ly["seq_h"], non_blocking=True)
-        rt.mla_decode(qd, ly["pool"], None, 128, 512, 64, td, sd, wl["topk"] or wl["ctx"],
-                      sparse_mla_top_k=wl["topk"], out=od, bmm1_scale=sm, bmm2_scale=1.0)
-        out_h.copy_(od, non_blocking=True)
-    e1.record()
-    e1.synchronize()
-    e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = kvb * e2e_steps * world / (float(e_ms.item()) / 1e3) / 1e9
+        call(ly)
+    e2e_serial = e2e_run(False)
+    e2e_value = e2e_run(True)
 
     # ---- the attention kernel alone: CUDA events recorded by the library immediately around
     # it (on its stream), over a separate run of the same steps
@@ -807,7 +846,9 @@ def main() -> None:
                          "step_frac_in_kernel": round(kernel_ms / (ms_max / args.steps), 3),
                          "splits": splits},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "pipeline": "copies of step k+1 / k-1 overlap the decode of step k (3 streams)",
+                    "serial_value": round(e2e_serial, 2)},
             "gpu_launches": args.steps * launches_per_step,
             "clocks": sampler.summary(t0, t1),
             "device_errors": errors,

@@ -42,6 +42,7 @@ _SYNC_FREE_T = int(os.environ.get("GLM53_NVFP4_SYNCFREE_T", "192"))
 # Persistent device buffers keyed like the reference's: ("shared", K, device index) for the
 # build_scratch buffer; ("err", index) / ("ws", index) for this module's own state.
 _bufs: dict = {}
+_ws_sizes: dict = {}   # decode workspace bytes per (batch, q_len, heads, max_seq_len, topk, device)
 
 
 def enabled() -> bool:
@@ -385,7 +386,11 @@ def _decode(query, kv_cache, workspace_buffer, kv_lora_rank, qk_rope_head_dim, b
         raise ValueError("out must be bf16 [B, q_len, H, 512] with a contiguous last dimension")
     dev = query.device
     with _on_device(dev):
-        ws_need = mla_decode_workspace_size(B, QL, H, max_seq_len, int(sparse_mla_top_k), dev)
+        size_key = (B, QL, H, int(max_seq_len), int(sparse_mla_top_k), dev.index)
+        ws_need = _ws_sizes.get(size_key)
+        if ws_need is None:                      # the plan depends only on these and the device
+            ws_need = mla_decode_workspace_size(B, QL, H, max_seq_len, int(sparse_mla_top_k), dev)
+            _ws_sizes[size_key] = ws_need
         ws = _workspace(dev, ws_need, workspace_buffer)
         args = [query.data_ptr(), query.stride(0), query.stride(1), query.stride(2),
                 pool.data_ptr(), pool.shape[0],
