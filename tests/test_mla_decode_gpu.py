@@ -162,7 +162,7 @@ def test_sparse_topk(rt, topk, pad):
     assert rt.device_errors() == 0
 
 
-def run_sparse(rt, B, H, topk, seq_lens, seed=5, qscale=1.0, pool_pages=256, bad=0.0, pad=0.0):
+def run_sparse(rt, B, H, topk, seq_lens, seed=5, qscale=1.0, pool_pages=256, bad=0.0, pad=0.0, QL=1):
     pool_t, pool = make_pool(pool_pages, seed=seed)
     R = pool_pages * 64
     g = torch.Generator().manual_seed(seed + 1)
@@ -172,7 +172,7 @@ def run_sparse(rt, B, H, topk, seq_lens, seed=5, qscale=1.0, pool_pages=256, bad
     nbad = torch.rand(B, topk, generator=g) < bad
     idx[nbad] = torch.where(torch.rand(B, topk, generator=g) < 0.5, R + 17, -5).to(torch.int32)[nbad]
     sl = torch.tensor(seq_lens, dtype=torch.int32)
-    q = (torch.randn(B, 1, H, 576, generator=g) * qscale).to(torch.bfloat16)
+    q = (torch.randn(B, QL, H, 576, generator=g) * qscale).to(torch.bfloat16)
     out = rt.mla_decode(q.cuda(), pool_t, None, 128, 512, 64, idx.view(B, 1, topk).cuda(), sl.cuda(), topk,
                         sparse_mla_top_k=topk, bmm1_scale=SM)
     ref = O.mla_decode(q.float(), pool, idx.view(B, 1, topk).numpy(), sl.numpy(), sparse=True, bmm1_scale=SM)
@@ -189,6 +189,14 @@ def test_sparse_many_tiles_per_split(rt):
 def test_sparse_peaked_scores(rt):
     out, ref = run_sparse(rt, 8, 64, 2048, [2048] * 4 + [1500] * 4, qscale=8.0, seed=11)
     check(out, ref, "sparse peaked")
+
+
+def test_sparse_rejects_multi_token_queries(rt):
+    """Sparse top-k tables hold one list per batch entry; a multi-token query (MTP) has one
+    top-k set per token, so callers pass tokens as batch entries.  q_len > 1 is refused."""
+    from glm53_flash_dual_dgx_spark_b200 import _lib
+    with pytest.raises(_lib.Nvfp4kvError, match="q_len == 1"):
+        run_sparse(rt, 2, 64, 256, [256, 100], QL=2)
 
 
 def test_sparse_out_of_range_indices_masked(rt):
