@@ -109,6 +109,10 @@ DecodePlan make_decode_plan(int batch, int q_len, int num_heads, int max_seq_len
     int want = units >= sms ? 1 : sms / units;
     want = want < 1 ? 1 : (want > kMaxSplits ? kMaxSplits : want);
     want = want > tiles ? tiles : want;
+    // the fewest splits with the same longest split: ceil(T / ceil(T / want)) (e.g. 64 tiles
+    // over at most 9 splits: 8 splits of 8, not 9 splits of 7-8), so fewer partials to merge
+    const int longest = (tiles + want - 1) / want;
+    want = (tiles + longest - 1) / longest;
     pl.tiles_total = tiles;
     pl.splits = want < 1 ? 1 : want;   // split sizes differ by at most one tile
     pl.part_bytes = pl.splits > 1

@@ -101,12 +101,13 @@ def test_workspace_size_formula():
     out = ctypes.c_size_t()
     qimg = 65536 + 8192 + 256                      # prepared Q of one 64-row query group
     assert lib.nvfp4kv_mla_decode_workspace_size(16, 1, 64, 8192, 0, ctypes.byref(out)) == _lib.OK
-    # 16 query groups on (at least) 148 SMs: 9 splits of 7-8 tiles; 64 rows x (512 + 2) floats
-    assert out.value == 9 * 16 * 64 * 514 * 4 + 16 * qimg
+    # 16 query groups on (at least) 148 SMs: up to 9 splits, and 8 of 8 tiles give the same
+    # longest split as 9 of 7-8; 64 rows x (512 + 2) floats per split
+    assert out.value == 8 * 16 * 64 * 514 * 4 + 16 * qimg
     assert lib.nvfp4kv_mla_decode_workspace_size(256, 1, 64, 8192, 0, ctypes.byref(out)) == _lib.OK
     assert out.value == 256 * qimg                 # enough query groups: no split partials
     assert lib.nvfp4kv_mla_decode_workspace_size(16, 1, 64, 0, 2048, ctypes.byref(out)) == _lib.OK
-    assert out.value == 9 * 16 * 64 * 514 * 4 + 16 * qimg   # sparse: 9 splits of 1-2 tiles
+    assert out.value == 8 * 16 * 64 * 514 * 4 + 16 * qimg   # sparse: 8 splits of 2 tiles
     assert lib.nvfp4kv_mla_decode_workspace_size(-1, 1, 64, 8192, 0, ctypes.byref(out)) == _lib.EINVAL
 
 
@@ -114,11 +115,11 @@ def test_decode_plan():
     lib = _lib.lib()
     splits, launches = ctypes.c_int(), ctypes.c_int()
     assert lib.nvfp4kv_mla_decode_plan(16, 1, 64, 8192, 0, ctypes.byref(splits), ctypes.byref(launches)) == _lib.OK
-    assert (splits.value, launches.value) == (9, 3)        # Q preparation + attention + combine
+    assert (splits.value, launches.value) == (8, 3)        # Q preparation + attention + combine
     assert lib.nvfp4kv_mla_decode_plan(256, 1, 64, 8192, 0, ctypes.byref(splits), ctypes.byref(launches)) == _lib.OK
     assert (splits.value, launches.value) == (1, 2)
     assert lib.nvfp4kv_mla_decode_plan(16, 1, 64, 0, 2048, ctypes.byref(splits), ctypes.byref(launches)) == _lib.OK
-    assert (splits.value, launches.value) == (9, 3)        # sparse: same three launches
+    assert (splits.value, launches.value) == (8, 3)        # sparse: same three launches
     assert lib.nvfp4kv_mla_decode_plan(1, 0, 64, 8192, 0, ctypes.byref(splits), ctypes.byref(launches)) == _lib.EINVAL
     assert lib.nvfp4kv_set_kernel_events(None, None) == _lib.OK
     assert lib.nvfp4kv_set_kernel_events(ctypes.c_void_p(1), None) == _lib.EINVAL
