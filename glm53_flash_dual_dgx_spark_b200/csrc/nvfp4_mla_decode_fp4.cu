@@ -300,22 +300,46 @@ __device__ __forceinline__ void load_rows_async(const Fp4Params& p, uint32_t slo
                                                 uint32_t* slot_mask, const int* sidx, bool staged,
                                                 int idx_base, int b, int tile_start, int end, int lane) {
     uint32_t live = 0;
+    if (staged) {
+        // the tile's 128 x 18 16-byte chunks numbered row-major; one instruction copies 32
+        // consecutive chunks (about two whole rows), so each row costs a few wide requests
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int r = 32 * k + lane;
-        const int pos = tile_start + r;
-        const int64_t row = pos < end ? token_row<true>(p, sidx, staged, idx_base, b, pos, true) : -1;
-        const bool ok = row >= 0;
-        live |= static_cast<uint32_t>(ok) << k;
-        const uint8_t* src = p.pool + (ok ? row : 0) * kRowBytes;
-        const uint32_t nbytes = ok ? 16u : 0u;
-        const uint32_t drow = slot_base + (r >> 3) * 1024 + (r & 7) * 128;
+        for (int k = 0; k < 4; ++k) {
+            const int pos = tile_start + 32 * k + lane;
+            const int64_t row = pos < end ? token_row<true>(p, sidx, true, idx_base, b, pos, true) : -1;
+            live |= static_cast<uint32_t>(row >= 0) << k;
+        }
+#pragma unroll 4
+        for (int i = 0; i < kTile * 18 / 32; ++i) {
+            const int c = 32 * i + lane;
+            const int r = c / 18, k = c - 18 * r;
+            const int pos = tile_start + r;
+            const int idx = pos < end ? sidx[pos - idx_base] : -1;
+            const bool ok = idx >= 0 && idx < p.pool_rows;
+            const uint8_t* src = p.pool + static_cast<int64_t>(ok ? idx : 0) * kRowBytes + 16 * k;
+            const uint32_t dst = k < 16 ? slot_base + (k >> 3) * 16384 + (r >> 3) * 1024 + (r & 7) * 128 +
+                                              (((k & 7) ^ (r & 7)) << 4)
+                                        : slot_base + kCodeBytes + r * 32 + 16 * (k - 16);
+            cp_async16_zfill(dst, src, ok ? 16u : 0u);
+        }
+    } else {
 #pragma unroll
-        for (int c = 0; c < 16; ++c)
-            cp_async16_zfill(drow + (c >> 3) * 16384 + (((c & 7) ^ (r & 7)) << 4), src + 16 * c, nbytes);
+        for (int k = 0; k < 4; ++k) {
+            const int r = 32 * k + lane;
+            const int pos = tile_start + r;
+            const int64_t row = pos < end ? token_row<true>(p, sidx, staged, idx_base, b, pos, true) : -1;
+            const bool ok = row >= 0;
+            live |= static_cast<uint32_t>(ok) << k;
+            const uint8_t* src = p.pool + (ok ? row : 0) * kRowBytes;
+            const uint32_t nbytes = ok ? 16u : 0u;
+            const uint32_t drow = slot_base + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
-            cp_async16_zfill(slot_base + kCodeBytes + r * 32 + 16 * h, src + 256 + 16 * h, nbytes);
+            for (int c = 0; c < 16; ++c)
+                cp_async16_zfill(drow + (c >> 3) * 16384 + (((c & 7) ^ (r & 7)) << 4), src + 16 * c, nbytes);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                cp_async16_zfill(slot_base + kCodeBytes + r * 32 + 16 * h, src + 256 + 16 * h, nbytes);
+        }
     }
     cp_async_mbar_arrive(bar_full);
 #pragma unroll
