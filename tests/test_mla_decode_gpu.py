@@ -180,8 +180,9 @@ def run_sparse(rt, B, H, topk, seq_lens, seed=5, qscale=1.0, pool_pages=256, bad
 
 
 def test_sparse_many_tiles_per_split(rt):
-    """20 entries x 128 heads = 40 query groups: 3 splits of ~11 tiles each, so the 2-slot
-    tile ring wraps many times; ragged counts end tiles mid-way."""
+    """20 entries x 128 heads = 40 query groups: 3 splits of ~11 tiles each, so the 3-slot
+    tile ring wraps many times and each split's ~1365 row ids exceed the 768 staged in
+    shared memory (the one-row-per-lane copy path); ragged counts end tiles mid-way."""
     out, ref = run_sparse(rt, 20, 128, 4096, [4096, 4000, 3001, 129] * 5)
     check(out, ref, "sparse many tiles")
 
