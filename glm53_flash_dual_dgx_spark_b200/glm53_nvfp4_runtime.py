@@ -38,6 +38,9 @@ _ON = os.environ.get("GLM53_NVFP4_KV", "0") == "1"          # read once at impor
 # Sync-free ceiling of build_scratch (runtime:134-140): steps with at most this many query
 # tokens gather every table entry into a persistent buffer (no host sync, graph-safe).
 _SYNC_FREE_T = int(os.environ.get("GLM53_NVFP4_SYNCFREE_T", "192"))
+# Opt-in: the T > _SYNC_FREE_T branch of build_scratch deduplicates on the device
+# (build_scratch_sync_free) instead of with torch.unique, so no step synchronises the host.
+_SYNC_FREE_DEDUP = os.environ.get("GLM53_NVFP4_SYNCFREE_DEDUP", "0") == "1"
 
 # Persistent device buffers keyed like the reference's: ("shared", K, device index) for the
 # build_scratch buffer; ("err", index) / ("ws", index) for this module's own state.
@@ -165,7 +168,9 @@ def build_scratch(kv_cache: torch.Tensor, block_tables: torch.Tensor):
     block_tables: [T, 1, K] int32 physical token rows (-1 padded).
     Returns (scratch [P, 64, 656] uint8, tables [T, 1, K] into scratch), as the reference
     (runtime:143-182): T <= _SYNC_FREE_T gathers every entry into a persistent buffer with
-    fixed shapes and no host sync; larger T deduplicates with torch.unique first.
+    fixed shapes and no host sync; larger T deduplicates with torch.unique first, or, with
+    GLM53_NVFP4_SYNCFREE_DEDUP=1, on the device without a host sync (the scratch then has
+    capacity-many pages; the consumer reads only the rows the tables name).
     """
     pool = kv_cache.view(-1, NV_BYTES)
     T, one, K = block_tables.shape
@@ -184,6 +189,9 @@ def build_scratch(kv_cache: torch.Tensor, block_tables: torch.Tensor):
         buf, ar = ent
         _gather(pool, flat, buf.view(-1, DS_BYTES)[:S])
         return buf[:P], ar[:S].view(T, 1, K)
+    if _SYNC_FREE_DEDUP:
+        scratch, tables, _ = build_scratch_sync_free(kv_cache, block_tables)
+        return scratch, tables
     uniq, inv = torch.unique(flat, return_inverse=True)
     S = uniq.shape[0]
     P = (S + 63) // 64

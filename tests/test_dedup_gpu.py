@@ -107,3 +107,24 @@ def test_dedup_flags_bad_entries_and_capacity(rt):
     ref_scratch, ref_tables = O.build_scratch(pool_np, bt)
     assert np.array_equal(tables.cpu().numpy(), ref_tables)
     assert np.array_equal(scratch.view(-1, 656)[:100].cpu().numpy(), ref_scratch.reshape(-1, 656)[:100])
+
+
+def test_build_scratch_opt_in_uses_the_device_dedup(rt, monkeypatch):
+    """GLM53_NVFP4_SYNCFREE_DEDUP=1 routes build_scratch's large-step branch to the device
+    dedup: same tables as the reference branch, its pages first, and no host sync."""
+    pool_np, pool = _pool(2048, seed=12)
+    bt = _tables(256, 32, 2048, seed=4, distinct=500)
+    ref_scratch, ref_tables = O.build_scratch(pool_np, bt)
+    monkeypatch.setattr(rt, "_SYNC_FREE_DEDUP", True)
+    btd = torch.from_numpy(bt).cuda()
+    rt.build_scratch(pool, btd)                          # allocates the workspace once
+    torch.cuda.synchronize()
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        scratch, tables = rt.build_scratch(pool, btd)
+    finally:
+        torch.cuda.set_sync_debug_mode("default")
+    assert np.array_equal(tables.cpu().numpy(), ref_tables)
+    P = ref_scratch.shape[0]
+    assert np.array_equal(scratch[:P].cpu().numpy(), ref_scratch)
+    assert rt.device_errors() == 0
