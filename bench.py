@@ -2,7 +2,7 @@
 """Benchmark of the NVFP4 paged KV-cache read path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
-                    [--workload dense8k|dense128k|sparse|long|append]
+                    [--workload dense8k|dense128k|sparse|long|append|dedup]
                     [--impl ours|reference]
 
 Default workload = BASELINE config 2: dense MLA decode over the 288-byte NVFP4 paged pool,
@@ -56,6 +56,12 @@ WORKLOADS = {
     "append": dict(desc="config 5 append: 16 seqs x 2048-token chunks per step quantised into a "
                         "2,713,846-token pool (42,404 pages of 64) at random free pages, 1 % outliers x20",
                    B=16, H=0, QL=0, ctx=2048, topk=0, pool_tokens=2713846),
+    # SURVEY 8(f) 1 on config 5's prefill: build_scratch's large-step branch (torch.unique in
+    # the reference) on the device: one step's block tables deduplicated and gathered to 656 B rows
+    "dedup": dict(desc="config 5 prefill step, build_scratch without a host sync: 2048 tokens x top-2048 "
+                       "entries from a 300,000-token context of a 2,713,846-token pool (10 % -1 padding), "
+                       "deduplicated on the device and gathered into 656 B rows",
+                  B=2048, H=0, QL=0, ctx=300000, topk=2048, pool_tokens=2713846, dedup=True),
     "long": dict(desc="config 4 (one layer): 5 x 460,000 + 3 x 900,000-token sequences, 64 heads, "
                       "MTP q_len 3, token-balanced sequence / page-range partition over the ranks",
                  B=8, H=64, QL=3, ctx=0, topk=0, lens=[460000] * 5 + [900000] * 3),
@@ -193,7 +199,13 @@ def make_layers(rt, torch, wl, layers, dev, seed):
 APPEND_BYTES_PER_TOKEN = 1024 + 288 + 8   # bf16 latent read, 288 B row written, int64 slot read
 
 
+DEDUP_ENTRY_BYTES = 4 + 4          # entry read, table written
+DEDUP_ROW_BYTES = NV_BYTES + 656    # distinct row read, 656 B row written
+
+
 def kv_bytes_per_step(wl) -> int:
+    if wl.get("dedup"):
+        raise ValueError("the dedup workload's bytes depend on its distinct entries (dedup_bytes)")
     if "pool_tokens" in wl:
         return wl["B"] * wl["ctx"] * APPEND_BYTES_PER_TOKEN
     if "lens" in wl:
@@ -289,6 +301,162 @@ def cpu_append_sample(seconds: float):
         if el >= seconds:
             break
     return runs * T * APPEND_BYTES_PER_TOKEN / el / 1e9, el / runs, T
+
+
+def dedup_tables(wl, seed):
+    """block_tables [T, 1, K] int32 of the dedup workload: entries uniform over a context window
+    of the pool, 10 % -1 padding."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    rows = wl["pool_tokens"] // 64 * 64
+    base = int(torch.randint(0, rows - wl["ctx"], (1,), generator=g))
+    bt = base + torch.randint(0, wl["ctx"], (wl["B"], 1, wl["topk"]), generator=g)
+    bt[torch.rand(bt.shape, generator=g) < 0.1] = -1
+    return bt.to(torch.int32)
+
+
+_CPU_SAMPLE: dict = {}
+
+
+def dedup_bytes(n_entries: int, n_unique: int) -> int:
+    return n_entries * DEDUP_ENTRY_BYTES + n_unique * DEDUP_ROW_BYTES
+
+
+def cpu_dedup_sample(wl, seconds: float):
+    """The oracle's large-step build_scratch (numpy unique + the C restatement of _gather_kernel)
+    on 64 of the workload's 2048 tokens, repeated for ~`seconds`; returns (GB/s, s per run, desc)."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    if "dedup" not in _CPU_SAMPLE:                   # inputs built once per process
+        bt = dedup_tables(wl, 0)[:64].numpy()
+        pool = np.zeros((wl["pool_tokens"] // 64 * 64, NV_BYTES), np.uint8)
+        pool[:, 256:] = 0x38
+        _CPU_SAMPLE["dedup"] = (bt, pool, len(np.unique(bt)))
+    bt, pool, n_unique = _CPU_SAMPLE["dedup"]
+    runs, t0 = 0, time.perf_counter()
+    while True:
+        O.build_scratch(pool, bt, sync_free_t=0)
+        runs += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    per = el / runs
+    return dedup_bytes(bt.size, n_unique) / per / 1e9, per, f"64 tokens x {wl['topk']} entries, {n_unique} distinct"
+
+
+def run_dedup(args, wl, rt, torch, dist, dev, rank, world, local):
+    """--workload dedup: build_scratch_sync_free on a config-5 prefill step (weak scaling)."""
+    rows = wl["pool_tokens"] // 64 * 64
+    pool = torch.zeros(rows // 64, 64, NV_BYTES, dtype=torch.uint8, device=dev)
+    pool[..., 256:] = 0x38                           # scale 1.0 in every block
+    tabs = [dedup_tables(wl, 1 + rank * 7 + k) for k in range(2)]
+    tabs_d = [t.to(dev) for t in tabs]
+    n_entries = tabs[0].numel()
+    cap = wl["ctx"] + 1                              # distinct entries: the context window and -1
+    outs = []
+    for t in tabs_d:                                 # eager warm-up (allocates the workspace)
+        outs.append(rt.build_scratch_sync_free(pool, t, capacity_rows=cap))
+    torch.cuda.synchronize()
+    n_unique = [int(o[2].item()) for o in outs]
+    step_bytes = sum(dedup_bytes(n_entries, u) for u in n_unique) / len(n_unique)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graphs = []
+    with torch.cuda.stream(s):
+        for t in tabs_d:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=s):
+                rt.build_scratch_sync_free(pool, t, capacity_rows=cap)
+            graphs.append(gr)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    soak_end = time.perf_counter() + 1.0
+    k = 0
+    while time.perf_counter() < soak_end or k < args.warmup:
+        graphs[k % 2].replay()
+        k += 1
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for k in range(args.steps):
+        graphs[k % 2].replay()
+    ev1.record()
+    ev1.synchronize()
+    t1 = time.perf_counter()
+    if world > 1:
+        dist.barrier()
+    sampler.stop()
+    t_max = torch.tensor([ev0.elapsed_time(ev1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    per_ms = float(t_max.item()) / args.steps
+    value = step_bytes * world / (per_ms / 1e3) / 1e9
+
+    # end to end through the public API: the block tables host->device, the inverse tables
+    # device->host, serial on one stream
+    e_steps = max(10, min(args.e2e_steps, 50))
+    bt_h = [t.pin_memory() for t in tabs]
+    tb_h = torch.empty(n_entries, dtype=torch.int32).pin_memory()
+    btd = torch.empty_like(tabs_d[0])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for k in range(e_steps):
+        btd.copy_(bt_h[k % 2], non_blocking=True)
+        _, tables, _ = rt.build_scratch_sync_free(pool, btd, capacity_rows=cap)
+        tb_h.copy_(tables.view(-1), non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = step_bytes * world * e_steps / (float(e_ms.item()) / 1e3) / 1e9
+    errors = rt.device_errors(dev)
+    if rank == 0:
+        peak, peak_kind = load_peaks()
+        achieved = step_bytes / (per_ms / 1e3) / 1e9
+        line = {
+            "metric": "sync-free dedup + 656 B gather GB/s (8 B per table entry, 944 B per distinct row)",
+            "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(per_ms, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic (seeded uniform top-k entries over a context window, 10 % -1)",
+            "config": {"workload": wl["desc"], "entries_per_step": n_entries,
+                       "distinct_per_step": n_unique, "pool_rows": rows,
+                       "l2": f"inputs larger than L2: {step_bytes / 2**20:.0f} MiB moved per step",
+                       "parallelism": f"a pool per rank x{world} (weak scaling)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": profile_traffic("dedup", "dedup_config5.md"),
+                         "per_launch_bytes": int(step_bytes), "kernel_ms": round(per_ms, 5),
+                         "kernel": "dedup_* (mark, block sums, scan, positions, tables, gather): the whole call",
+                         "step_frac_in_kernel": 1.0},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": n_entries * 4,
+                    "d2h_bytes_per_step": n_entries * 4, "steps": e_steps},
+            "gpu_launches": args.steps * 6,
+            "clocks": sampler.summary(t0, t1),
+            "device_errors": errors,
+        }
+        if world == 1:
+            gbs, per, desc = cpu_dedup_sample(wl, args.cpu_seconds)
+            line["cpu_baseline"] = {
+                "value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                "sample": f"oracle build_scratch large-step branch (numpy unique + C gather) on {desc}, "
+                          f"repeated for ~{args.cpu_seconds:.0f} s ({per * 1e3:.1f} ms each; {cpu_model()})"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_append(args, wl, rt, torch, dist, dev, rank, world, local):
@@ -632,6 +800,27 @@ def reference_arm(args, wl):
     import numpy as np  # noqa: F401
 
     cores = os.cpu_count()
+    if wl.get("dedup"):
+        cpu_dedup_sample(wl, 0.0)
+        times = []
+        for i in range(args.warmup + args.steps):
+            gbs, per, desc = cpu_dedup_sample(wl, 0.0)
+            if i >= args.warmup:
+                times.append((gbs, per))
+        gbs = sum(g for g, _ in times) / len(times)
+        per = sum(p for _, p in times) / len(times)
+        line = {"impl": "reference",
+                "metric": "sync-free dedup + 656 B gather GB/s (8 B per table entry, 944 B per distinct row)",
+                "value": round(gbs, 4), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(per * 1e3, 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+                "data": "synthetic (seeded uniform top-k entries over a context window, 10 % -1)",
+                "config": {"workload": wl["desc"], "parallelism": f"a pool per rank x{args.gpus}"},
+                "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                                 "sample": f"oracle build_scratch large-step branch on {desc} ({cpu_model()})"},
+                "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     append = "pool_tokens" in wl
     sample_fn = (lambda: cpu_append_sample(0.0)) if append else (lambda: cpu_decode_sample(wl, 0.0))
     sample_fn()                                    # warm: build oracle, fault pages in
@@ -700,6 +889,9 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     if "lens" in wl:
         run_long(args, wl, rt, torch, dist, dev, rank, world, local)
+        return
+    if wl.get("dedup"):
+        run_dedup(args, wl, rt, torch, dist, dev, rank, world, local)
         return
     if "pool_tokens" in wl:
         run_append(args, wl, rt, torch, dist, dev, rank, world, local)
