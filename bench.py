@@ -437,7 +437,7 @@ def run_dedup(args, wl, rt, torch, dist, dev, rank, world, local):
                        "parallelism": f"a pool per rank x{world} (weak scaling)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": profile_traffic("dedup", "dedup_config5.md"),
+                         "traffic": None,   # per kernel: profiles/dedup_config5.md
                          "per_launch_bytes": int(step_bytes), "kernel_ms": round(per_ms, 5),
                          "kernel": "dedup_* (mark, block sums, scan, positions, tables, gather): the whole call",
                          "step_frac_in_kernel": 1.0},
