@@ -215,8 +215,10 @@ def kv_bytes_per_step(wl) -> int:
 
 
 # pieces per rank of the long workload: one call's split plan is uniform over its units, so
-# the rank's tokens are cut into this many equal ranges (40 x 3 query groups fill 120-144 SMs)
-LONG_PIECES_PER_RANK = 40
+# the rank's tokens are cut into this many equal ranges.  Each call decodes one CTA per
+# (piece, query group); 48 pieces x 3 groups keep every call at <= 144 CTAs on 1-8 ranks
+# (partition.plan adds a unit where a cut crosses a sequence end), one wave on 148 SMs
+LONG_PIECES_PER_RANK = 48
 
 
 def make_long_step(rt, torch, wl, dev, rank, world, seed):
