@@ -92,11 +92,22 @@ __device__ __forceinline__ int64_t dedup_key(int32_t e, int64_t R, int32_t* err)
     return static_cast<int64_t>(e) + 1;
 }
 
+// Key 0 (every -1 entry, typically ~10 % of a step's table) is recorded once per block
+// through a shared flag: stores to one word serialise in L2.
 __global__ void __launch_bounds__(256)
 dedup_mark_kernel(const int32_t* __restrict__ entries, int64_t n, int64_t R, int32_t* __restrict__ marks,
                   int32_t* __restrict__ err) {
+    __shared__ int any_minus_one;
+    if (threadIdx.x == 0) any_minus_one = 0;
+    __syncthreads();
     const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (j < n) marks[dedup_key(entries[j], R, err)] = 1;
+    if (j < n) {
+        const int64_t key = dedup_key(entries[j], R, err);
+        if (key == 0) any_minus_one = 1;
+        else marks[key] = 1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && any_minus_one) marks[0] = 1;
 }
 
 // Block-wide exclusive scan of one value per thread; returns this thread's prefix and sets
