@@ -21,27 +21,38 @@ __device__ __forceinline__ float e2m1_value(uint32_t code) {
     return (code & 8u) ? __fsub_rn(0.0f, mag) : mag;
 }
 
-// Decode one lane's block: 8 code bytes (16 elements) times the block scale, in fp32.
-__device__ __forceinline__ void decode_block(uint2 codes, uint8_t scale_byte, float (&v)[16]) {
+// The 16 code values e2m1_value(c) in shared memory, filled by the block's first 16 threads
+// (every thread of the block calls this before any of them returns).  Looking a code up costs a
+// shared-memory load instead of the ~10 integer operations of building its value from bits,
+// which bound these kernels by the ALU pipe.
+__device__ __forceinline__ void fill_code_table(float* table) {
+    if (threadIdx.x < 16) table[threadIdx.x] = e2m1_value(threadIdx.x);
+    __syncthreads();
+}
+
+// Decode one lane's block: 8 code bytes (16 elements) times the block scale, in fp32; the
+// product of the exact table value and the scale, as the reference computes it.
+__device__ __forceinline__ void decode_block(uint2 codes, uint8_t scale_byte, const float* table,
+                                             float (&v)[16]) {
     const float s = e4m3_to_f32(scale_byte);
     const uint32_t w[2] = {codes.x, codes.y};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-        v[2 * i] = __fmul_rn(e2m1_value(byte & 15u), s);
-        v[2 * i + 1] = __fmul_rn(e2m1_value(byte >> 4), s);
+        v[2 * i] = __fmul_rn(table[byte & 15u], s);
+        v[2 * i + 1] = __fmul_rn(table[byte >> 4], s);
     }
 }
 
 // runtime:87-122.  One warp: the 656-byte row at `dst` re-encodes pool row clamp(src, 0, R-1).
 __device__ __forceinline__ void gather_row_ds656(const uint8_t* __restrict__ pool, int64_t R, int64_t src,
-                                                 uint8_t* __restrict__ dst, int lane) {
+                                                 const float* table, uint8_t* __restrict__ dst, int lane) {
     src = src < 0 ? 0 : (src > R - 1 ? R - 1 : src);          // :98
     const uint8_t* row = pool + src * kRowBytes;
     const uint2 codes = ldg_nc_v2(row + 8 * lane);
     const uint8_t sb = row[256 + lane];
     float v[16];
-    decode_block(codes, sb, v);                                 // :99-108
+    decode_block(codes, sb, table, v);                          // :99-108
     float amax = 0.0f;                                          // :109-112 (max includes 0.0)
 #pragma unroll
     for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fmaxf(fabsf(v[2 * i]), fabsf(v[2 * i + 1])));
@@ -53,11 +64,12 @@ __device__ __forceinline__ void gather_row_ds656(const uint8_t* __restrict__ poo
     uint32_t o[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        uint32_t w = 0;
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-            w |= static_cast<uint32_t>(f32_to_e4m3(__fmul_rn(v[4 * j + k], inv))) << (8 * k);
-        o[j] = w;
+        // two values per conversion (round to nearest even, saturating; .x -> low byte)
+        const uint32_t lo = __nv_cvt_float2_to_fp8x2(
+            make_float2(__fmul_rn(v[4 * j], inv), __fmul_rn(v[4 * j + 1], inv)), __NV_SATFINITE, __NV_E4M3);
+        const uint32_t hi = __nv_cvt_float2_to_fp8x2(
+            make_float2(__fmul_rn(v[4 * j + 2], inv), __fmul_rn(v[4 * j + 3], inv)), __NV_SATFINITE, __NV_E4M3);
+        o[j] = (lo & 0xFFFFu) | (hi << 16);
     }
     *reinterpret_cast<uint4*>(dst + 16 * lane) = make_uint4(o[0], o[1], o[2], o[3]);  // :117-120
     if ((lane & 7) == 0) *reinterpret_cast<float*>(dst + 512 + 4 * (lane >> 3)) = gscale;  // :114
@@ -68,10 +80,12 @@ __device__ __forceinline__ void gather_row_ds656(const uint8_t* __restrict__ poo
 __global__ void __launch_bounds__(256)
 gather_ds656_kernel(const uint8_t* __restrict__ pool, int64_t R, const int32_t* __restrict__ idx,
                     int64_t S, uint8_t* __restrict__ out) {
+    __shared__ float table[16];
+    fill_code_table(table);
     const int lane = threadIdx.x & 31;
     const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r >= S) return;
-    gather_row_ds656(pool, R, idx[r], out + r * kDsBytes, lane);
+    gather_row_ds656(pool, R, idx[r], table, out + r * kDsBytes, lane);
 }
 
 // ------------------------------------------------------------------ sync-free dedup
@@ -204,6 +218,8 @@ __global__ void __launch_bounds__(256)
 dedup_gather_kernel(const uint8_t* __restrict__ pool, int64_t R, const int32_t* __restrict__ uniq,
                     const int32_t* __restrict__ n_unique, uint8_t* __restrict__ scratch, int64_t cap,
                     int32_t* __restrict__ err) {
+    __shared__ float table[16];
+    fill_code_table(table);
     const int lane = threadIdx.x & 31;
     const int64_t nu = *n_unique;
     const int64_t padded = (nu + 63) / 64 * 64;
@@ -214,7 +230,7 @@ dedup_gather_kernel(const uint8_t* __restrict__ pool, int64_t R, const int32_t* 
          u += warps) {
         uint8_t* dst = scratch + u * kDsBytes;
         if (u < nu) {
-            gather_row_ds656(pool, R, uniq[u], dst, lane);
+            gather_row_ds656(pool, R, uniq[u], table, dst, lane);
         } else {
             reinterpret_cast<uint4*>(dst)[lane] = make_uint4(0u, 0u, 0u, 0u);   // 512 B
             if (lane < 9) reinterpret_cast<uint4*>(dst + 512)[lane] = make_uint4(0u, 0u, 0u, 0u);
@@ -238,6 +254,8 @@ template <int IDT>
 __global__ void __launch_bounds__(256)
 dequant_bf16_kernel(const uint8_t* __restrict__ pool, int64_t R, const void* __restrict__ rows,
                     int64_t n, __nv_bfloat16* __restrict__ out, int32_t* __restrict__ err) {
+    __shared__ float table[16];
+    fill_code_table(table);
     const int lane = threadIdx.x & 31;
     const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r >= n) return;
@@ -248,7 +266,7 @@ dequant_bf16_kernel(const uint8_t* __restrict__ pool, int64_t R, const void* __r
     if (src >= 0 && src < R) {
         const uint8_t* row = pool + src * kRowBytes;
         float v[16];
-        decode_block(ldg_nc_v2(row + 8 * lane), row[256 + lane], v);
+        decode_block(ldg_nc_v2(row + 8 * lane), row[256 + lane], table, v);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);  // exact
