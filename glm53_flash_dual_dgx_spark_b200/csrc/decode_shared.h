@@ -63,6 +63,14 @@ cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+// Argument checks of nvfp4kv_mla_decode that need no workspace (pointers, alignment, shape,
+// page geometry); `page_shift` receives log2(page_size) in dense mode.  No device call.
+int check_decode_args(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,
+                      const uint8_t* pool, int64_t pool_rows, const int32_t* tables, const int32_t* seq_lens,
+                      int batch, int q_len, int num_heads, int head_dim_qk, int kv_lora_rank, int sparse_topk,
+                      int page_size, int max_seq_len, const void* out, int64_t out_stride_b,
+                      int64_t out_stride_q, int64_t out_stride_h, int* page_shift);
+
 // Q preparation + the fused decode kernel (QK^T on the block-scaled fp4 tensor-core path),
 // paged (sparse_topk == 0) or top-k rows (sparse_topk > 0).
 int launch_decode_fp4(const DecodeArgs& a, const DecodePlan& pl, cudaStream_t st);

@@ -174,17 +174,13 @@ extern "C" int nvfp4kv_mla_decode_plan(int batch, int q_len, int num_heads, int 
 }
 
 namespace nvfp4kv {
-namespace {
 
-int decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,
-                const uint8_t* pool, int64_t pool_rows, const int32_t* tables, int64_t tables_stride,
-                const int32_t* seq_lens, int batch, int q_len, int num_heads, int head_dim_qk,
-                int kv_lora_rank, int sparse_topk, int page_size, int max_seq_len, float bmm1_scale,
-                float bmm2_scale, void* out, int64_t out_stride_b, int64_t out_stride_q,
-                int64_t out_stride_h, float* lse, void* workspace, size_t workspace_bytes,
-                int32_t* err_flag, nvfp4kv_stream_t stream) {
+int check_decode_args(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,
+                      const uint8_t* pool, int64_t pool_rows, const int32_t* tables, const int32_t* seq_lens,
+                      int batch, int q_len, int num_heads, int head_dim_qk, int kv_lora_rank, int sparse_topk,
+                      int page_size, int max_seq_len, const void* out, int64_t out_stride_b,
+                      int64_t out_stride_q, int64_t out_stride_h, int* page_shift_out) {
     if (batch < 0) return fail(NVFP4KV_EINVAL, "mla_decode: batch < 0");
-    if (batch == 0) return NVFP4KV_OK;
     if (!q || !pool || !tables || !seq_lens || !out)
         return fail(NVFP4KV_EINVAL, "mla_decode: null pointer");
     if (kv_lora_rank != NVFP4KV_LATENT)
@@ -211,6 +207,26 @@ int decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q
         return fail(NVFP4KV_EINVAL, "mla_decode: pool/q must be 16-byte aligned and q strides multiples of 8");
     if (reinterpret_cast<uintptr_t>(out) % 16 || out_stride_b % 8 || out_stride_q % 8 || out_stride_h % 8)
         return fail(NVFP4KV_EINVAL, "mla_decode: out must be 16-byte aligned and its strides multiples of 8");
+    if (page_shift_out) *page_shift_out = page_shift;
+    return NVFP4KV_OK;
+}
+
+namespace {
+
+int decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,
+                const uint8_t* pool, int64_t pool_rows, const int32_t* tables, int64_t tables_stride,
+                const int32_t* seq_lens, int batch, int q_len, int num_heads, int head_dim_qk,
+                int kv_lora_rank, int sparse_topk, int page_size, int max_seq_len, float bmm1_scale,
+                float bmm2_scale, void* out, int64_t out_stride_b, int64_t out_stride_q,
+                int64_t out_stride_h, float* lse, void* workspace, size_t workspace_bytes,
+                int32_t* err_flag, nvfp4kv_stream_t stream) {
+    if (batch < 0) return fail(NVFP4KV_EINVAL, "mla_decode: batch < 0");
+    if (batch == 0) return NVFP4KV_OK;
+    int page_shift = 0;
+    int rc = check_decode_args(q, q_stride_b, q_stride_q, q_stride_h, pool, pool_rows, tables, seq_lens, batch,
+                               q_len, num_heads, head_dim_qk, kv_lora_rank, sparse_topk, page_size, max_seq_len,
+                               out, out_stride_b, out_stride_q, out_stride_h, &page_shift);
+    if (rc != NVFP4KV_OK) return rc;
     const DecodePlan pl = make_decode_plan(batch, q_len, num_heads, max_seq_len, sparse_topk);
     if (!workspace || workspace_bytes < pl.ws_bytes)
         return fail(NVFP4KV_EWORKSPACE, "mla_decode: workspace %zu bytes < %zu required",
@@ -222,7 +238,6 @@ int decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q
     float* part_ml = pl.splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + part_o_bytes) : nullptr;
 
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    int rc;
     {
         DecodeArgs a{};
         a.q = q; a.q_sb = q_stride_b; a.q_sq = q_stride_q; a.q_sh = q_stride_h;

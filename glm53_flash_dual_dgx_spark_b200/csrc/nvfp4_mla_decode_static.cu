@@ -24,12 +24,16 @@
 //     non-zero, before the combine kernel reads them; the Q preparation kernel writes every
 //     byte of the prepared-Q images before the attention kernel reads them;
 //   - the first call on each device looks up the array's address (cudaGetSymbolAddress,
-//     with that device current).  Make that first call before any stream capture begins.
+//     with that device current) and keeps it for the life of the process.  Make that first
+//     call before any stream capture begins.  A cudaDeviceReset (or any re-creation of the
+//     device's primary context) reloads the module and may move the array, so the library
+//     must not be used on a device after it has been reset.
 #include <cuda_runtime.h>
 
 #include <mutex>
 
 #include "abi_common.h"
+#include "decode_shared.h"
 
 namespace nvfp4kv {
 namespace {
@@ -77,8 +81,13 @@ extern "C" int nvfp4kv_mla_decode_static(const void* q, int64_t q_stride_b, int6
     using namespace nvfp4kv;
     if (batch < 0) return fail(NVFP4KV_EINVAL, "mla_decode_static: batch < 0");
     if (batch == 0) return NVFP4KV_OK;
+    // the argument errors of nvfp4kv_mla_decode come first, then the capacity
+    int rc = check_decode_args(q, q_stride_b, q_stride_q, q_stride_h, pool, pool_rows, tables, seq_lens, batch,
+                               q_len, num_heads, head_dim_qk, kv_lora_rank, sparse_topk, page_size, max_seq_len,
+                               out, out_stride_b, out_stride_q, out_stride_h, nullptr);
+    if (rc != NVFP4KV_OK) return rc;
     size_t need = 0;
-    int rc = nvfp4kv_mla_decode_workspace_size(batch, q_len, num_heads, max_seq_len, sparse_topk, &need);
+    rc = nvfp4kv_mla_decode_workspace_size(batch, q_len, num_heads, max_seq_len, sparse_topk, &need);
     if (rc != NVFP4KV_OK) return rc;
     if (need > kStaticScratchBytes)
         return fail(NVFP4KV_EWORKSPACE,

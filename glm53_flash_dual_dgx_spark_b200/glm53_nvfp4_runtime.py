@@ -38,9 +38,14 @@ _ON = os.environ.get("GLM53_NVFP4_KV", "0") == "1"          # read once at impor
 # Sync-free ceiling of build_scratch (runtime:134-140): steps with at most this many query
 # tokens gather every table entry into a persistent buffer (no host sync, graph-safe).
 _SYNC_FREE_T = int(os.environ.get("GLM53_NVFP4_SYNCFREE_T", "192"))
-# Opt-in: the T > _SYNC_FREE_T branch of build_scratch deduplicates on the device
-# (build_scratch_sync_free) instead of with torch.unique, so no step synchronises the host.
-_SYNC_FREE_DEDUP = os.environ.get("GLM53_NVFP4_SYNCFREE_DEDUP", "0") == "1"
+# The T > _SYNC_FREE_T branch of build_scratch deduplicates on the device
+# (build_scratch_sync_free), so no step synchronises the host.  GLM53_NVFP4_UNIQUE=1 restores
+# the reference's torch.unique branch (runtime:177-182), which synchronises to size its output.
+_UNIQUE = os.environ.get("GLM53_NVFP4_UNIQUE", "0") == "1"
+# Rows of the device branch's persistent scratch (656 B each).  0 (default): min(T * K, pool
+# rows + 1), the most distinct entries a step can have; a smaller bound caps the memory, and a
+# step with more distinct entries than it sets NVFP4KV_DEVERR_CAPACITY.
+_SYNC_FREE_ROWS = int(os.environ.get("GLM53_NVFP4_SYNCFREE_ROWS", "0"))
 
 # Persistent device buffers keyed like the reference's: ("shared", K, device index) for the
 # build_scratch buffer; ("err", index) / ("ws", index) for this module's own state.
@@ -168,9 +173,11 @@ def build_scratch(kv_cache: torch.Tensor, block_tables: torch.Tensor):
     block_tables: [T, 1, K] int32 physical token rows (-1 padded).
     Returns (scratch [P, 64, 656] uint8, tables [T, 1, K] into scratch), as the reference
     (runtime:143-182): T <= _SYNC_FREE_T gathers every entry into a persistent buffer with
-    fixed shapes and no host sync; larger T deduplicates with torch.unique first, or, with
-    GLM53_NVFP4_SYNCFREE_DEDUP=1, on the device without a host sync (the scratch then has
-    capacity-many pages; the consumer reads only the rows the tables name).
+    fixed shapes and no host sync.  Larger T deduplicates on the device without a host sync
+    (build_scratch_sync_free): the tables equal the reference's, and the reference's
+    ceil(n_unique / 64) pages are the first pages of a persistent capacity-sized scratch (the
+    consumer reads only the rows the tables name).  With GLM53_NVFP4_UNIQUE=1 the large branch
+    is the reference's torch.unique one, which synchronises the host.
     """
     pool = kv_cache.view(-1, NV_BYTES)
     T, one, K = block_tables.shape
@@ -189,8 +196,9 @@ def build_scratch(kv_cache: torch.Tensor, block_tables: torch.Tensor):
         buf, ar = ent
         _gather(pool, flat, buf.view(-1, DS_BYTES)[:S])
         return buf[:P], ar[:S].view(T, 1, K)
-    if _SYNC_FREE_DEDUP:
-        scratch, tables, _ = build_scratch_sync_free(kv_cache, block_tables)
+    if not _UNIQUE:
+        scratch, tables, _ = build_scratch_sync_free(kv_cache, block_tables,
+                                                     capacity_rows=_SYNC_FREE_ROWS or None)
         return scratch, tables
     uniq, inv = torch.unique(flat, return_inverse=True)
     S = uniq.shape[0]
@@ -213,6 +221,10 @@ def build_scratch_sync_free(kv_cache: torch.Tensor, block_tables: torch.Tensor,
     (rows from n_unique to the end of that page are zero); later pages are not written.
     P_cap covers capacity_rows rows, by default min(T * K, pool rows + 1), the most distinct
     entries there can be; fewer rows than the distinct entries set NVFP4KV_DEVERR_CAPACITY.
+    The scratch is a view of one persistent buffer per device, allocated when a call needs
+    more rows than it holds (656 B per row; for a 2,713,846-row pool and 2048 x 2048 entries
+    the default capacity is 2,713,847 rows = 1.78 GB) and overwritten by the next call, like
+    the reference's persistent sync-free buffer.
     """
     pool = kv_cache.view(-1, NV_BYTES)
     _require_cuda(pool, "kv_cache")
@@ -230,7 +242,13 @@ def build_scratch_sync_free(kv_cache: torch.Tensor, block_tables: torch.Tensor,
         raise ValueError("capacity_rows must be >= 0")
     dev = pool.device
     P = (cap + 63) // 64
-    scratch = torch.empty(P, 64, DS_BYTES, dtype=torch.uint8, device=dev)
+    skey = ("dedup_scratch", dev.index)
+    buf = _bufs.get(skey)
+    if buf is None or buf.shape[0] < P:
+        _bufs.pop(skey, None)
+        buf = torch.empty(P, 64, DS_BYTES, dtype=torch.uint8, device=dev)
+        _bufs[skey] = buf
+    scratch = buf[:P]
     tables = torch.empty(n, dtype=torch.int32, device=dev)
     n_unique = torch.empty(1, dtype=torch.int32, device=dev)
     ints = ctypes.c_int64()

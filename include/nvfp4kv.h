@@ -212,8 +212,10 @@ int nvfp4kv_selftest_bounded_wait(int32_t* err_flag, nvfp4kv_stream_t stream);
  *   - NVFP4KV_EWORKSPACE if nvfp4kv_mla_decode_workspace_size() of the shape exceeds the
  *     scratch (on a 148-SM device: calls with more than 453 query groups of 64 rows,
  *     e.g. batch > 453 at 64 heads and q_len 1);
- *   - the first call on a device looks up the scratch address with that device current;
- *     make it before any stream capture begins;
+ *   - argument errors (EINVAL) are reported before the capacity check (EWORKSPACE);
+ *   - the first call on a device looks up the scratch address with that device current and
+ *     keeps it for the life of the process; make it before any stream capture begins, and do
+ *     not use the library on a device after a cudaDeviceReset (the array may move);
  *   - one scratch per device: calls whose kernels overlap on a device race on it.
  */
 int nvfp4kv_mla_decode_static(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,

@@ -74,6 +74,34 @@ def test_gather_and_decode_argument_checks_without_launch():
     assert b"workspace" in lib.nvfp4kv_last_error()
 
 
+def test_static_decode_rejects_oversized_shapes_without_launch():
+    """nvfp4kv_mla_decode_static: argument errors come first, then the 32 MiB capacity.  At 64
+    heads and q_len 1 the prepared Q (72.25 KB per 64-row query group) exceeds the scratch
+    from 454 groups on; neither path reaches a device call."""
+    lib = _lib.lib()
+    cap = 33554432
+    qimg = 65536 + 8192 + 256
+    size = ctypes.c_size_t()
+    assert lib.nvfp4kv_mla_decode_workspace_size(453, 1, 64, 8192, 0, ctypes.byref(size)) == _lib.OK
+    assert size.value == 453 * qimg <= cap
+    assert lib.nvfp4kv_mla_decode_workspace_size(454, 1, 64, 8192, 0, ctypes.byref(size)) == _lib.OK
+    assert size.value == 454 * qimg > cap
+
+    def call(B, q=4096, pool=4096, R=512):
+        # (q, strides, pool, rows, tables, tstride, seq_lens, B, q_len, H, D, R, topk, page, max_seq,
+        #  s1, s2, out, out strides, err, stream): 16-byte aligned fake pointers, never dereferenced
+        return lib.nvfp4kv_mla_decode_static(q, 64 * 576, 64 * 576, 576, pool, 1024, 64, 128, 64,
+                                             B, 1, 64, 576, R, 0, 64, 8192, 1.0, 1.0,
+                                             4096, 64 * 512, 64 * 512, 512, None, None)
+
+    assert call(0) == _lib.OK
+    assert call(454) == _lib.EWORKSPACE
+    assert b"static scratch" in lib.nvfp4kv_last_error()
+    assert call(454, q=None) == _lib.EINVAL           # a null pointer is reported, not the capacity
+    assert call(454, pool=4100) == _lib.EINVAL        # so is a misaligned pool
+    assert call(454, R=256) == _lib.EINVAL
+
+
 def test_dedup_workspace_and_argument_checks_without_launch():
     lib = _lib.lib()
     ints = ctypes.c_int64()

@@ -109,13 +109,14 @@ def test_dedup_flags_bad_entries_and_capacity(rt):
     assert np.array_equal(scratch.view(-1, 656)[:100].cpu().numpy(), ref_scratch.reshape(-1, 656)[:100])
 
 
-def test_build_scratch_opt_in_uses_the_device_dedup(rt, monkeypatch):
-    """GLM53_NVFP4_SYNCFREE_DEDUP=1 routes build_scratch's large-step branch to the device
-    dedup: same tables as the reference branch, its pages first, and no host sync."""
+def test_build_scratch_large_step_uses_the_device_dedup(rt, monkeypatch):
+    """build_scratch's large-step branch is the device dedup by default (GLM53_NVFP4_UNIQUE=1
+    selects torch.unique): same tables as the reference branch, its pages first, no host
+    sync, and a persistent scratch that later calls reuse instead of allocating."""
     pool_np, pool = _pool(2048, seed=12)
     bt = _tables(256, 32, 2048, seed=4, distinct=500)
     ref_scratch, ref_tables = O.build_scratch(pool_np, bt)
-    monkeypatch.setattr(rt, "_SYNC_FREE_DEDUP", True)
+    monkeypatch.setattr(rt, "_UNIQUE", False)
     btd = torch.from_numpy(bt).cuda()
     rt.build_scratch(pool, btd)                          # allocates the workspace once
     torch.cuda.synchronize()
@@ -127,4 +128,12 @@ def test_build_scratch_opt_in_uses_the_device_dedup(rt, monkeypatch):
     assert np.array_equal(tables.cpu().numpy(), ref_tables)
     P = ref_scratch.shape[0]
     assert np.array_equal(scratch[:P].cpu().numpy(), ref_scratch)
+    assert rt.device_errors() == 0
+    again, _ = rt.build_scratch(pool, btd)
+    assert again.data_ptr() == scratch.data_ptr()        # the persistent buffer, not a new one
+    monkeypatch.setattr(rt, "_SYNC_FREE_ROWS", 512)      # a capped scratch: 500 distinct rows fit
+    capped, tables = rt.build_scratch(pool, btd)
+    assert capped.shape[0] == 8
+    assert np.array_equal(tables.cpu().numpy(), ref_tables)
+    assert np.array_equal(capped[:P].cpu().numpy(), ref_scratch)
     assert rt.device_errors() == 0

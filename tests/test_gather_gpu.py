@@ -40,14 +40,14 @@ def test_build_scratch_matches_reference_golden(rt, T):
     sa, ta = rt.build_scratch(pool, bt)
     assert np.array_equal(sa.cpu().numpy(), s[f"sync_scratch_{T}"])
     assert np.array_equal(ta.cpu().numpy(), s[f"sync_tables_{T}"])
-    saved = rt._SYNC_FREE_T
-    rt._SYNC_FREE_T = 0
-    try:
-        sb, tb = rt.build_scratch(pool, bt)
-    finally:
-        rt._SYNC_FREE_T = saved
-    assert np.array_equal(sb.cpu().numpy(), s[f"uniq_scratch_{T}"])
-    assert np.array_equal(tb.cpu().numpy(), s[f"uniq_tables_{T}"])
+    for unique in (True, False):
+        sb, tb = _large_step_path(rt, pool, bt, unique)
+        ref = s[f"uniq_scratch_{T}"]
+        if unique:                                   # the reference's torch.unique branch
+            assert np.array_equal(sb.cpu().numpy(), ref)
+        else:                                        # device dedup: its pages come first
+            assert np.array_equal(sb[:ref.shape[0]].cpu().numpy(), ref)
+        assert np.array_equal(tb.cpu().numpy(), s[f"uniq_tables_{T}"])
 
 
 POOL_ROWS = 100_000
@@ -59,13 +59,15 @@ def random_pool():
     return torch.randint(0, 256, (POOL_ROWS, 288), dtype=torch.uint8, device="cuda")
 
 
-def _unique_path(rt, pool, tables):
-    saved = rt._SYNC_FREE_T
-    rt._SYNC_FREE_T = 0
+def _large_step_path(rt, pool, tables, unique):
+    """build_scratch's T > _SYNC_FREE_T branch: torch.unique (unique=True, the reference's)
+    or the default device dedup."""
+    saved = rt._SYNC_FREE_T, rt._UNIQUE
+    rt._SYNC_FREE_T, rt._UNIQUE = 0, unique
     try:
         return rt.build_scratch(pool, tables)
     finally:
-        rt._SYNC_FREE_T = saved
+        rt._SYNC_FREE_T, rt._UNIQUE = saved
 
 
 @pytest.mark.parametrize("T,K", [(1, 64), (3, 64), (17, 64), (64, 64), (65, 64), (100, 64), (192, 64),
@@ -77,10 +79,11 @@ def test_sync_free_equals_unique_path(rt, random_pool, T, K):
     idx[:, :, : K // 4] = idx[:1, :, : K // 4]
     idx[torch.rand(T, 1, K, device="cuda") < 0.1] = -1
     sa, ta = rt.build_scratch(random_pool, idx)
-    sb, tb = _unique_path(rt, random_pool, idx)
     fa = sa.reshape(-1, 656)[ta.view(-1).long()]
-    fb = sb.reshape(-1, 656)[tb.view(-1).long()]
-    assert torch.equal(fa, fb)
+    for unique in (True, False):
+        sb, tb = _large_step_path(rt, random_pool, idx, unique)
+        fb = sb.reshape(-1, 656)[tb.view(-1).long()]
+        assert torch.equal(fa, fb)
     if T * K <= 20000:
         ref = O.gather_ds656(random_pool.cpu().numpy(), idx.view(-1).cpu().numpy())
         assert np.array_equal(fa.cpu().numpy(), ref)

@@ -3,7 +3,8 @@ argument) against nvfp4kv_mla_decode with a caller workspace, both called throug
 
 Two static calls in a row must each match the workspace entry point within the decode
 tolerance (rtol 2e-2, atol 1e-2); they run the same kernels with the same split plan, so
-they are expected to agree bit for bit as well.  The file is named to be collected last and
+they are expected to agree bit for bit as well.  After a warm-up call, the two calls must
+leave the device's free memory unchanged (nothing is allocated).  The file is named to be collected last and
 builds all of its inputs itself, so it passes alone in a fresh process or after other tests.
 """
 import ctypes
@@ -68,14 +69,21 @@ def test_static_scratch_matches_workspace_entry_point(B, H, ctx, num_pages, spar
     _lib.check(lib.nvfp4kv_mla_decode(*_common_args(q, pool, tables, seq_lens, B, H, ctx, sparse_topk, ref),
                                       ctypes.c_void_p(ws.data_ptr()), size.value,
                                       ctypes.c_void_p(err.data_ptr()), stream), "mla_decode")
-    outs = []
-    for _ in range(2):
-        out = torch.full((B, 1, H, 512), float("nan"), dtype=torch.bfloat16, device="cuda")
+    # warm-up call: the first one on a device looks up the scratch array (and, with lazy module
+    # loading, may load the module that holds it); every call after it must allocate nothing
+    warm = torch.empty(B, 1, H, 512, dtype=torch.bfloat16, device="cuda")
+    _lib.check(lib.nvfp4kv_mla_decode_static(*_common_args(q, pool, tables, seq_lens, B, H, ctx, sparse_topk, warm),
+                                             ctypes.c_void_p(err.data_ptr()), stream), "mla_decode_static")
+    outs = [torch.full((B, 1, H, 512), float("nan"), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    for out in outs:
         _lib.check(lib.nvfp4kv_mla_decode_static(*_common_args(q, pool, tables, seq_lens, B, H, ctx,
                                                                sparse_topk, out),
                                                  ctypes.c_void_p(err.data_ptr()), stream),
                    "mla_decode_static")
-        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free_before, "a static call changed the device's free memory"
     torch.cuda.synchronize()
     assert int(err.item()) == 0
     r = ref.float().cpu().numpy()
