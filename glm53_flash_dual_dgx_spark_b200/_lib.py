@@ -18,6 +18,7 @@ OK, EINVAL, EWORKSPACE, ECUDA = 0, 1, 2, 3
 DEVERR_TIMEOUT, DEVERR_BAD_SLOT, DEVERR_BAD_INDEX, DEVERR_BAD_PAGE, DEVERR_SEQ_LEN = 1, 2, 4, 8, 16
 DEVERR_CAPACITY = 32
 DTYPE_BF16, DTYPE_F16 = 0, 1
+DIV_IEEE, DIV_TRITON = 0, 1
 INDEX_I64, INDEX_I32 = 0, 1
 
 # Every symbol include/nvfp4kv.h declares, with its ctypes signature.
@@ -27,6 +28,8 @@ SIGNATURES = {
     "nvfp4kv_last_error": (ctypes.c_char_p, []),
     "nvfp4kv_append": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, _I, _P, _P]),
     "nvfp4kv_gather_ds656": (_I, [_P, _I64, _P, _I64, _P, _P]),
+    "nvfp4kv_set_gather_division": (_I, [_I]),
+    "nvfp4kv_get_gather_division": (_I, []),
     "nvfp4kv_dequant_bf16": (_I, [_P, _I64, _P, _I, _I64, _P, _P, _P]),
     "nvfp4kv_dedup_gather_ds656": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I64, _P, _P, _P]),
     "nvfp4kv_dedup_workspace_ints": (_I, [_I64, _I64, ctypes.POINTER(_I64)]),

@@ -1,6 +1,8 @@
 // Pool-row readers: the 656-byte fp8_ds_mla gather (byte-identical to the reference's
 // _gather_kernel) and a bf16 dequantiser.  Both are HBM-bound; one warp handles one row,
 // each lane one 16-element scale block (8 code bytes + 1 scale byte).
+#include <atomic>
+
 #include "abi_common.h"
 #include "common.cuh"
 
@@ -44,7 +46,19 @@ __device__ __forceinline__ void decode_block(uint2 codes, uint8_t scale_byte, co
     }
 }
 
+// a / b with the PTX instruction div.full.f32, which is what GPU Triton emits for an fp32 `/`
+// (checked on the B200 against the reference's own compiled `amax / 448.0` and `1.0 / gscale`,
+// every one of 500,882 quotients equal).  Used only in the Triton-division mode.
+__device__ __forceinline__ float div_full(float a, float b) {
+    float d;
+    asm("div.full.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+
 // runtime:87-122.  One warp: the 656-byte row at `dst` re-encodes pool row clamp(src, 0, R-1).
+// kTritonDiv = false divides exactly (IEEE: the reference run on the CPU); true divides as the
+// reference compiled by Triton for the GPU does (div.full.f32), byte for byte.
+template <bool kTritonDiv>
 __device__ __forceinline__ void gather_row_ds656(const uint8_t* __restrict__ pool, int64_t R, int64_t src,
                                                  const float* table, uint8_t* __restrict__ dst, int lane) {
     src = src < 0 ? 0 : (src > R - 1 ? R - 1 : src);          // :98
@@ -59,8 +73,8 @@ __device__ __forceinline__ void gather_row_ds656(const uint8_t* __restrict__ poo
     amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
     amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));  // 8 lanes = 128 elements
-    const float gscale = fmaxf(__fdiv_rn(amax, 448.0f), 1e-12f);  // :113
-    const float inv = __fdiv_rn(1.0f, gscale);                     // :115-116
+    const float gscale = fmaxf(kTritonDiv ? div_full(amax, 448.0f) : __fdiv_rn(amax, 448.0f), 1e-12f);  // :113
+    const float inv = kTritonDiv ? div_full(1.0f, gscale) : __fdiv_rn(1.0f, gscale);                    // :115-116
     uint32_t o[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -77,6 +91,7 @@ __device__ __forceinline__ void gather_row_ds656(const uint8_t* __restrict__ poo
 }
 
 // Row r of `out` re-encodes pool row clamp(idx[r], 0, R-1).
+template <bool kTritonDiv>
 __global__ void __launch_bounds__(256)
 gather_ds656_kernel(const uint8_t* __restrict__ pool, int64_t R, const int32_t* __restrict__ idx,
                     int64_t S, uint8_t* __restrict__ out) {
@@ -85,7 +100,7 @@ gather_ds656_kernel(const uint8_t* __restrict__ pool, int64_t R, const int32_t* 
     const int lane = threadIdx.x & 31;
     const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r >= S) return;
-    gather_row_ds656(pool, R, idx[r], table, out + r * kDsBytes, lane);
+    gather_row_ds656<kTritonDiv>(pool, R, idx[r], table, out + r * kDsBytes, lane);
 }
 
 // ------------------------------------------------------------------ sync-free dedup
@@ -214,6 +229,7 @@ dedup_tables_kernel(const int32_t* __restrict__ entries, int64_t n, int64_t R, c
 
 // Warp u (grid-stride) writes scratch row u: the gathered row of distinct value u for
 // u < n_unique, zeros up to the next multiple of 64 rows, within `cap` rows.
+template <bool kTritonDiv>
 __global__ void __launch_bounds__(256)
 dedup_gather_kernel(const uint8_t* __restrict__ pool, int64_t R, const int32_t* __restrict__ uniq,
                     const int32_t* __restrict__ n_unique, uint8_t* __restrict__ scratch, int64_t cap,
@@ -230,7 +246,7 @@ dedup_gather_kernel(const uint8_t* __restrict__ pool, int64_t R, const int32_t* 
          u += warps) {
         uint8_t* dst = scratch + u * kDsBytes;
         if (u < nu) {
-            gather_row_ds656(pool, R, uniq[u], table, dst, lane);
+            gather_row_ds656<kTritonDiv>(pool, R, uniq[u], table, dst, lane);
         } else {
             reinterpret_cast<uint4*>(dst)[lane] = make_uint4(0u, 0u, 0u, 0u);   // 512 B
             if (lane < 9) reinterpret_cast<uint4*>(dst + 512)[lane] = make_uint4(0u, 0u, 0u, 0u);
@@ -280,8 +296,22 @@ dequant_bf16_kernel(const uint8_t* __restrict__ pool, int64_t R, const void* __r
     dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
 }
 
+// Division mode of the 656-byte row encoders (nvfp4kv_set_gather_division), process-wide.
+std::atomic<int> g_gather_division{NVFP4KV_DIV_IEEE};
+
 }  // namespace
 }  // namespace nvfp4kv
+
+extern "C" int nvfp4kv_set_gather_division(int mode) {
+    using namespace nvfp4kv;
+    if (mode != NVFP4KV_DIV_IEEE && mode != NVFP4KV_DIV_TRITON)
+        return fail(NVFP4KV_EINVAL, "set_gather_division: mode must be NVFP4KV_DIV_IEEE or NVFP4KV_DIV_TRITON (got %d)",
+                    mode);
+    g_gather_division.store(mode);
+    return NVFP4KV_OK;
+}
+
+extern "C" int nvfp4kv_get_gather_division(void) { return nvfp4kv::g_gather_division.load(); }
 
 extern "C" int nvfp4kv_gather_ds656(const uint8_t* pool, int64_t pool_rows, const int32_t* idx,
                                     int64_t num_rows, uint8_t* out, nvfp4kv_stream_t stream) {
@@ -294,8 +324,11 @@ extern "C" int nvfp4kv_gather_ds656(const uint8_t* pool, int64_t pool_rows, cons
         return fail(NVFP4KV_EINVAL, "nvfp4kv_gather_ds656: pool and out must be 16-byte aligned");
     const int warps = 8;
     const dim3 grid(static_cast<unsigned>((num_rows + warps - 1) / warps));
-    gather_ds656_kernel<<<grid, warps * 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        pool, pool_rows, idx, num_rows, out);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (g_gather_division.load() == NVFP4KV_DIV_TRITON)
+        gather_ds656_kernel<true><<<grid, warps * 32, 0, st>>>(pool, pool_rows, idx, num_rows, out);
+    else
+        gather_ds656_kernel<false><<<grid, warps * 32, 0, st>>>(pool, pool_rows, idx, num_rows, out);
     return check_launch("nvfp4kv_gather_ds656");
 }
 
@@ -373,7 +406,12 @@ extern "C" int nvfp4kv_dedup_gather_ds656(const uint8_t* pool, int64_t pool_rows
     if (scratch_rows > 0) {
         const int64_t want = (scratch_rows + 7) / 8;   // 8 warps a block, one row each per pass
         const unsigned grid = static_cast<unsigned>(want < 148 * 16 ? want : 148 * 16);
-        dedup_gather_kernel<<<grid, 256, 0, st>>>(pool, pool_rows, uniq, n_unique, scratch, scratch_rows, err_flag);
+        if (g_gather_division.load() == NVFP4KV_DIV_TRITON)
+            dedup_gather_kernel<true><<<grid, 256, 0, st>>>(pool, pool_rows, uniq, n_unique, scratch, scratch_rows,
+                                                            err_flag);
+        else
+            dedup_gather_kernel<false><<<grid, 256, 0, st>>>(pool, pool_rows, uniq, n_unique, scratch, scratch_rows,
+                                                             err_flag);
         if ((rc = check_launch("nvfp4kv_dedup_gather_ds656 (gather)")) != NVFP4KV_OK) return rc;
     }
     return NVFP4KV_OK;

@@ -47,6 +47,11 @@ _UNIQUE = os.environ.get("GLM53_NVFP4_UNIQUE", "0") == "1"
 # step with more distinct entries than it sets NVFP4KV_DEVERR_CAPACITY.
 _SYNC_FREE_ROWS = int(os.environ.get("GLM53_NVFP4_SYNCFREE_ROWS", "0"))
 
+# Division of the 656 B row encoders (_gather, build_scratch): "ieee" (default) gives the
+# reference's rows as it computes on the CPU, "triton" its rows as Triton compiles it for the
+# GPU (approximate fp32 division), byte for byte.  See set_gather_division.
+_GATHER_DIV = os.environ.get("GLM53_NVFP4_GATHER_DIV", "ieee")
+
 # Persistent device buffers keyed like the reference's: ("shared", K, device index) for the
 # build_scratch buffer; ("err", index) / ("ws", index) for this module's own state.
 _bufs: dict = {}
@@ -150,6 +155,25 @@ def write_nvfp4(kv_c: torch.Tensor, kv_cache: torch.Tensor, slot_mapping: torch.
 
 
 # ------------------------------------------------------------------ 656-byte read path
+def set_gather_division(mode: str) -> None:
+    """Division of the 656-byte row encoders, process-wide: "ieee" (exact; the reference's
+    _gather_kernel as it computes on the CPU) or "triton" (div.full.f32, the approximate fp32
+    division GPU Triton compiles the reference's `amax / 448.0` and `1.0 / gscale` to, so the
+    rows are byte-identical to the reference's GPU output).  No counterpart in the reference."""
+    modes = {"ieee": _lib.DIV_IEEE, "triton": _lib.DIV_TRITON}
+    if mode not in modes:
+        raise ValueError(f"gather division must be 'ieee' or 'triton', got {mode!r}")
+    _lib.check(_lib.lib().nvfp4kv_set_gather_division(modes[mode]), "nvfp4kv_set_gather_division")
+
+
+def get_gather_division() -> str:
+    return "triton" if _lib.lib().nvfp4kv_get_gather_division() == _lib.DIV_TRITON else "ieee"
+
+
+if _GATHER_DIV != "ieee":
+    set_gather_division(_GATHER_DIV)
+
+
 def _gather(pool: torch.Tensor, idx: torch.Tensor, out: torch.Tensor) -> None:
     """NVFP4 pool rows at idx -> fp8_ds_mla 656-byte rows in out (runtime:128-131)."""
     S = idx.shape[0]

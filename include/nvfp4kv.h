@@ -88,6 +88,24 @@ int nvfp4kv_gather_ds656(const uint8_t* pool, int64_t pool_rows, const int32_t* 
                          int64_t num_rows, uint8_t* out, nvfp4kv_stream_t stream);
 
 /*
+ * Division used by the 656-byte row encoders (nvfp4kv_gather_ds656, nvfp4kv_dedup_gather_ds656)
+ * for the reference's two fp32 quotients, gscale = max(amax / 448, 1e-12) and 1 / gscale
+ * (nvfp4-kv/glm53_nvfp4_runtime.py:113-116):
+ *   NVFP4KV_DIV_IEEE   (default) exact division: the reference's kernel as run on the CPU
+ *                      (the Triton interpreter computes in IEEE fp32);
+ *   NVFP4KV_DIV_TRITON the reference's kernel as Triton compiles it for the GPU, whose fp32 `/`
+ *                      is the approximate div.full.f32: rows byte-identical to it.
+ * The two differ in the last bit of about half of the fp32 scales and, where a value lands on
+ * an e4m3 rounding tie, in that e4m3 byte.  Process-wide; set it once before launching.  The
+ * append (nvfp4kv_append) gives the same bytes under both (no input can sit between the two
+ * quotients' roundings there), so it has no mode.  No counterpart in the reference.
+ */
+#define NVFP4KV_DIV_IEEE 0
+#define NVFP4KV_DIV_TRITON 1
+int nvfp4kv_set_gather_division(int mode);
+int nvfp4kv_get_gather_division(void);
+
+/*
  * Sync-free deduplicating gather: the T > _SYNC_FREE_T branch of build_scratch
  * (nvfp4-kv/glm53_nvfp4_runtime.py:177-182: torch.unique(flat, return_inverse=True) then
  * _gather into a zeroed [ceil(S/64), 64, 656] scratch) without the host synchronisation

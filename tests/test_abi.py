@@ -21,10 +21,22 @@ def declared_functions():
 def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     names = declared_functions()
-    assert len(names) == 14, names
+    assert len(names) == 16, names
     for n in names:
         assert hasattr(lib, n), n
     assert set(names) == set(_lib.SIGNATURES)
+
+
+def test_gather_division_mode_switch_without_launch():
+    lib = _lib.lib()
+    assert lib.nvfp4kv_get_gather_division() == _lib.DIV_IEEE          # the default
+    assert lib.nvfp4kv_set_gather_division(7) == _lib.EINVAL
+    assert b"NVFP4KV_DIV" in lib.nvfp4kv_last_error()
+    try:
+        assert lib.nvfp4kv_set_gather_division(_lib.DIV_TRITON) == _lib.OK
+        assert lib.nvfp4kv_get_gather_division() == _lib.DIV_TRITON
+    finally:
+        assert lib.nvfp4kv_set_gather_division(_lib.DIV_IEEE) == _lib.OK
 
 
 def test_version_and_empty_error():
