@@ -76,18 +76,14 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic(workload: str, summary: str = ""):
-    """Per-launch DRAM bytes of the workload's kernel from a committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", summary or f"mla_decode_{workload}.md")
+def profile_traffic(workload: str):
+    """DRAM bytes per launch of the workload's dominant kernel from profiles/traffic.json (one
+    ncu capture each, with the command that made it), or None when none was captured."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
     if not os.path.exists(p):
         return None
-    for line in open(p):
-        if line.strip().startswith("traffic_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].strip())
-            except ValueError:
-                return None
-    return None
+    ent = json.load(open(p)).get("workloads", {}).get(workload)
+    return float(ent["bytes_per_launch"]) if ent else None
 
 
 def cpu_model() -> str:
@@ -439,7 +435,7 @@ def run_dedup(args, wl, rt, torch, dist, dev, rank, world, local):
                        "parallelism": f"a pool per rank x{world} (weak scaling)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": None,   # per kernel: profiles/dedup_config5.md
+                         "traffic": profile_traffic("dedup"),
                          "per_launch_bytes": int(step_bytes), "kernel_ms": round(per_ms, 5),
                          "kernel": "dedup_* (mark, block sums, scan, positions, tables, gather): the whole call",
                          "step_frac_in_kernel": 1.0},
@@ -450,6 +446,7 @@ def run_dedup(args, wl, rt, torch, dist, dev, rank, world, local):
             "device_errors": errors,
         }
         if world == 1:
+            line["gpu_reference"] = gpu_reference_dedup(torch, pool, tabs_d, per_ms * 1e3)
             gbs, per, desc = cpu_dedup_sample(wl, args.cpu_seconds)
             line["cpu_baseline"] = {
                 "value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
@@ -601,7 +598,7 @@ def run_append(args, wl, rt, torch, dist, dev, rank, world, local):
             "tokens_per_s": round(T * world / (per_ms / 1e3), 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": profile_traffic("append", "append_config5.md"),
+                         "traffic": profile_traffic("append"),
                          "per_launch_bytes": step_bytes, "kernel_ms": round(per_ms, 5),
                          "kernel": "append_kernel", "step_frac_in_kernel": 1.0},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
@@ -614,6 +611,7 @@ def run_append(args, wl, rt, torch, dist, dev, rank, world, local):
             "device_errors": errors,
         }
         if world == 1:
+            line["gpu_reference"] = gpu_reference_append(torch, inputs, pages * 64, dev, per_ms * 1e3)
             gbs, per, n = cpu_append_sample(args.cpu_seconds)
             line["cpu_baseline"] = {
                 "value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
@@ -857,6 +855,239 @@ def reference_arm(args, wl):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------- the reference on the GPU
+REF_RUNTIME = os.environ.get("GLM53_REFERENCE_RUNTIME",
+                             os.path.join(ROOT, "baseline", "_ref", "nvfp4-kv", "glm53_nvfp4_runtime.py"))
+
+
+def load_reference_runtime():
+    """The reference's own runtime module (unmodified, from its install under baseline/_ref), or
+    (None, reason)."""
+    import importlib.util
+
+    if not os.path.exists(REF_RUNTIME):
+        return None, f"reference runtime not installed at {REF_RUNTIME}"
+    try:
+        spec = importlib.util.spec_from_file_location("glm53_reference_runtime", REF_RUNTIME)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return mod, None
+    except Exception as e:  # noqa: BLE001
+        return None, f"reference runtime failed to import: {e!r}"[:300]
+
+
+def graph_time_us(torch, fns, steps, warm=3):
+    """Mean device time of fns[k % len(fns)]() replayed from CUDA graphs (one per fn), CUDA events
+    on the replay stream; eager if a capture fails."""
+    for f in fns:
+        for _ in range(warm):
+            f()
+    torch.cuda.synchronize()
+    graphs, mode = [], "cuda graphs"
+    try:
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            for f in fns:
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=st):
+                    f()
+                graphs.append(gr)
+        torch.cuda.current_stream().wait_stream(st)
+        torch.cuda.synchronize()
+        run = [g.replay for g in graphs]
+    except Exception:  # noqa: BLE001
+        graphs, run, mode = [], fns, "eager"
+        torch.cuda.synchronize()
+    for k in range(2 * len(run)):
+        run[k % len(run)]()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for k in range(steps):
+        run[k % len(run)]()
+    b.record()
+    b.synchronize()
+    del graphs
+    return a.elapsed_time(b) / steps * 1e3, mode
+
+
+def gpu_reference_decode(torch, wl, L, dev, ours_us):
+    """The reference's read path on this GPU for the same layers: its build_scratch (Triton
+    _gather_kernel into 656 B fp8_ds_mla rows, runtime:143-176) followed by a stock B200 consumer
+    of those rows, vLLM's FlashMLA sparse fp8 decode (the fork's FlashInfer consumer of the
+    656 B rows is not in this image; FlashInfer 0.6.11's trtllm-gen MLA takes only 576 B rows)."""
+    ref, why = load_reference_runtime()
+    if ref is None:
+        return {"unavailable": why}
+    B, ctx, topk = wl["B"], wl["ctx"], wl["topk"]
+    K = topk or ctx
+    sm = 1.0 / math.sqrt(576)
+    rec = {"path": "reference build_scratch (Triton _gather_kernel, 656 B rows) -> FlashMLA sparse fp8 decode "
+                   "(vLLM 0.22) on those rows", "config": f"batch {B}, {K} rows per sequence"}
+    rows = []
+    for ly in L:
+        if topk:
+            rows.append(ly["tables"].view(B, 1, topk))
+        else:
+            pos = torch.arange(ctx, device=dev)
+            pt = ly["tables"].long()
+            rows.append((pt[:, pos // 64] * 64 + pos % 64).to(torch.int32).view(B, 1, ctx))
+    ref._bufs.clear()
+    try:
+        g_us, mode = graph_time_us(torch, [lambda i=i: ref.build_scratch(L[i]["pool"], rows[i]) for i in range(len(L))],
+                                   50 if K > 8192 else 400)
+        rec["gather_us"], rec["timing"] = round(g_us, 2), mode
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"reference gather failed: {e!r}"[:300]}
+    rec["gather_bytes_per_step"] = B * K * (NV_BYTES + 656)
+    if K > 8192:
+        rec["consumer"] = ("not run: FlashMLA's sparse decode at top-k %d is outside its design point; the "
+                           "reference gather alone bounds the path from below" % K)
+        rec["step_us_lower_bound"] = rec["gather_us"]
+        rec["ours_step_us"] = round(ours_us, 2)
+        rec["speedup_at_least"] = round(rec["gather_us"] / ours_us, 2)
+        return rec
+    try:
+        from vllm.third_party.flashmla.flash_mla_interface import flash_mla_with_kvcache, get_mla_metadata
+
+        metas = [get_mla_metadata()[0] for _ in L]
+
+        def consume(i, scratch, tables):
+            return flash_mla_with_kvcache(q=L[i]["q"], k_cache=scratch.view(-1, 64, 1, 656), block_table=None,
+                                          cache_seqlens=None, head_dim_v=512, tile_scheduler_metadata=metas[i],
+                                          is_fp8_kvcache=True, indices=tables.view(B, 1, K), softmax_scale=sm)[0]
+
+        def full(i):
+            scratch, tables = ref.build_scratch(L[i]["pool"], rows[i])
+            return consume(i, scratch, tables)
+
+        f_us, mode = graph_time_us(torch, [lambda i=i: full(i) for i in range(len(L))], 400)
+        rec["step_us"] = round(f_us, 2)
+        rec["consumer_us"] = round(max(f_us - rec["gather_us"], 0.0), 2)
+        rec["ours_step_us"] = round(ours_us, 2)
+        rec["speedup"] = round(f_us / ours_us, 2)
+        rec["timing"] = mode
+        # the consumer's accuracy on these rows, against the exact dequantised attention
+        o = full(0).float().view(B, wl["H"], 512)
+        kv = _exact_rows(torch, L[0], rows[0][0, 0])
+        qf = L[0]["q"][0, 0, :, :512].float()
+        tru = torch.softmax(qf @ kv.t() * sm, dim=-1) @ kv
+        rec["consumer_rel_err_seq0"] = round(float((o[0] - tru).norm() / tru.norm()), 4)
+        rec["note"] = ("FlashMLA's output on these rows does not match the fp8_ds_mla format "
+                       "(consumer_rel_err_seq0; also on rows written by vLLM's own concat_and_cache_mla), so its "
+                       "time stands in for the fork's consumer, not its numbers")
+    except Exception as e:  # noqa: BLE001
+        rec["consumer"] = f"unavailable: {e!r}"[:300]
+        rec["step_us_lower_bound"] = rec["gather_us"]
+        rec["speedup_at_least"] = round(rec["gather_us"] / ours_us, 2)
+    return rec
+
+
+def _exact_rows(torch, ly, rows):
+    from glm53_flash_dual_dgx_spark_b200 import glm53_nvfp4_runtime as rt
+
+    return rt.dequant(ly["pool"], rows.to(torch.int32)).float()
+
+
+def gpu_reference_append(torch, inputs, pool_rows, dev, ours_us):
+    """The reference's write_nvfp4 (its Triton _quant_kernel, runtime:37-76) on the same chunks."""
+    ref, why = load_reference_runtime()
+    if ref is None:
+        return {"unavailable": why}
+    pool = torch.zeros(pool_rows, NV_BYTES, dtype=torch.uint8, device=dev)
+    try:
+        us, mode = graph_time_us(torch, [lambda inp=inp: ref.write_nvfp4(inp["x"], pool, inp["slots"])
+                                         for inp in inputs], 200)
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"reference append failed: {e!r}"[:300]}
+    return {"path": "reference write_nvfp4 (Triton _quant_kernel)", "step_us": round(us, 3), "timing": mode,
+            "ours_step_us": round(ours_us, 3), "speedup": round(us / ours_us, 2)}
+
+
+def gpu_reference_dedup(torch, pool, tabs_d, ours_us):
+    """The reference's large-step build_scratch (torch.unique + its Triton gather, runtime:177-182),
+    eager: torch.unique synchronises with the host to size its output."""
+    ref, why = load_reference_runtime()
+    if ref is None:
+        return {"unavailable": why}
+    try:
+        for t in tabs_d:
+            ref.build_scratch(pool, t)
+        torch.cuda.synchronize()
+        n = 20
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        a.record()
+        for k in range(n):
+            ref.build_scratch(pool, tabs_d[k % len(tabs_d)])
+        b.record()
+        b.synchronize()
+        wall = (time.perf_counter() - t0) / n * 1e6
+        us = a.elapsed_time(b) / n * 1e3
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"reference build_scratch failed: {e!r}"[:300]}
+    return {"path": "reference build_scratch large-step branch (torch.unique + Triton gather, host sync)",
+            "step_us": round(us, 2), "wall_us": round(wall, 2), "timing": "eager (the branch synchronises)",
+            "ours_step_us": round(ours_us, 2), "speedup": round(us / ours_us, 2)}
+
+
+# ---------------------------------------------------------------------------- checks of the results
+def fp32_check(torch, rt, wl, ly, seqs, sm):
+    """Layer `ly`'s decode output for sequences `seqs` against the exact dequantised attention in
+    fp32: (max over them of rel L2, whether every element is within 2e-2 rel / 1e-2 abs)."""
+    B, H, ctx, topk = wl["B"], wl["H"], wl["ctx"], wl["topk"]
+    worst, ok = 0.0, True
+    for b in seqs:
+        if topk:
+            rows = ly["tables"].view(B, topk)[b]
+        else:
+            pos = torch.arange(ctx, device=ly["q"].device)
+            rows = ly["tables"][b].long()[pos // 64] * 64 + pos % 64
+        kv = rt.dequant(ly["pool"], rows.to(torch.int32)).float()
+        qf = ly["q"][b, 0, :, :512].float()
+        tru = torch.softmax(qf @ kv.t() * sm, dim=-1) @ kv
+        o = ly["out"][b, 0].float()
+        worst = max(worst, float((o - tru).norm() / tru.norm()))
+        ok = ok and bool(((o - tru).abs() <= 1e-2 + 2e-2 * tru.abs()).all())
+    return worst, ok
+
+
+def check_ranks(torch, rt, dist, wl, L, dev, rank, world, call, sm):
+    """After timing: every rank's layer-0 output is all-gathered over NCCL, and rank 0 rebuilds each
+    other rank's layer 0 from its seed, decodes it itself and compares (same kernels and inputs:
+    expected bit-identical; the gate is 2e-2 rel / 1e-2 abs).  Every rank also checks two of its
+    own sequences against the exact fp32 attention.  Returns the record (rank 0) and whether every
+    check passed (all ranks agree on it)."""
+    rel, ok_fp32 = fp32_check(torch, rt, wl, L[0], [0, wl["B"] - 1], sm)
+    rec = {"fp32_rel_l2_max": round(rel, 5), "fp32_within_tol": ok_fp32}
+    ok = ok_fp32
+    if world > 1:
+        gathered = [torch.empty_like(L[0]["out"]) for _ in range(world)]
+        dist.all_gather(gathered, L[0]["out"])
+        torch.cuda.synchronize()
+        if rank == 0:
+            max_diff, identical, within = 0.0, True, True
+            for r in range(1, world):
+                lr = make_layers(rt, torch, wl, 1, dev, seed=1 + r)[0]
+                call(lr)
+                torch.cuda.synchronize()
+                got, mine = gathered[r].float(), lr["out"].float()
+                max_diff = max(max_diff, float((got - mine).abs().max()))
+                identical = identical and bool(torch.equal(gathered[r], lr["out"]))
+                within = within and bool(((got - mine).abs() <= 1e-2 + 2e-2 * mine.abs()).all())
+                del lr
+                torch.cuda.empty_cache()
+            rec.update({"ranks_rechecked_on_rank0": world - 1, "max_abs_diff": max_diff,
+                        "bit_identical": identical, "within_tol": within})
+            ok = ok and within
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        ok = bool(flag.item())
+    rec["passed"] = ok
+    return rec, ok
+
+
 # ---------------------------------------------------------------------------- GPU side
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -1049,11 +1280,9 @@ def main() -> None:
         dist.all_reduce(k_ms, op=dist.ReduceOp.MAX)
     kernel_ms = float(k_ms.item())
 
-    # ---- outputs of every rank gathered once, after timing (the only collective)
-    if world > 1:
-        gathered = [torch.empty_like(L[0]["out"]) for _ in range(world)]
-        dist.all_gather(gathered, L[0]["out"])
-        torch.cuda.synchronize()
+    # ---- outputs of every rank gathered once, after timing (the only data collective), and
+    # checked: rank 0 decodes every other rank's layer 0 itself and compares
+    check, passed = check_ranks(torch, rt, dist, wl, L, dev, rank, world, call, sm)
 
     errors = rt.device_errors(dev)
     if rank == 0:
@@ -1087,7 +1316,9 @@ def main() -> None:
             "clocks": sampler.summary(t0, t1),
             "device_errors": errors,
         }
+        line["result_check"] = check
         if world == 1:
+            line["gpu_reference"] = gpu_reference_decode(torch, wl, L, dev, ms_max / args.steps * 1e3)
             gbs, per, ctx = cpu_decode_sample(wl, args.cpu_seconds)
             line["cpu_baseline"] = {
                 "value": round(gbs, 4), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
@@ -1099,6 +1330,8 @@ def main() -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if not passed:
+        sys.exit("result check failed: a rank's output is outside 2e-2 rel / 1e-2 abs")
 
 
 if __name__ == "__main__":

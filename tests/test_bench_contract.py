@@ -2,7 +2,7 @@
 
 The workloads carry BASELINE.json's shapes, the algorithmic bytes per step follow the metric's
 definition (288 B per attended token row per query group; 1320 B per appended token), the ncu
-traffic figures the bench reports are the ones committed under profiles/, and the reference
+traffic figures the bench reports are the ones committed in profiles/traffic.json, and the reference
 arm (the CPU oracle port, runnable here) prints the one JSON line the driver parses.
 """
 import json
@@ -38,7 +38,8 @@ def test_reported_traffic_comes_from_the_committed_profiles():
     for wl in ("dense8k", "dense128k", "sparse"):
         t = bench.profile_traffic(wl)
         assert t is not None and t > bench.kv_bytes_per_step(bench.WORKLOADS[wl]) * 0.9, wl
-    assert bench.profile_traffic("append", "append_config5.md") > 0
+    assert bench.profile_traffic("append") > 0
+    assert bench.profile_traffic("no-such-workload") is None
 
 
 @pytest.mark.parametrize("workload", ["dense8k", "append"])
