@@ -56,16 +56,30 @@ WORKLOADS = {
     "append": dict(desc="config 5 append: 16 seqs x 2048-token chunks per step quantised into a "
                         "2,713,846-token pool (42,404 pages of 64) at random free pages, 1 % outliers x20",
                    B=16, H=0, QL=0, ctx=2048, topk=0, pool_tokens=2713846),
-    # SURVEY 8(f) 1 on config 5's prefill: build_scratch's large-step branch (torch.unique in
+    # config 5's prefill scratch: build_scratch's large-step branch (torch.unique in
     # the reference) on the device: one step's block tables deduplicated and gathered to 656 B rows
     "dedup": dict(desc="config 5 prefill step, build_scratch without a host sync: 2048 tokens x top-2048 "
                        "entries from a 300,000-token context of a 2,713,846-token pool (10 % -1 padding), "
                        "deduplicated on the device and gathered into 656 B rows",
                   B=2048, H=0, QL=0, ctx=300000, topk=2048, pool_tokens=2713846, dedup=True),
+    # config 5's attention half, as the reference's large-step read path runs it: every new token
+    # attends the top-2048 rows its indexer picks from its causal window (the prior 300,000
+    # tokens of its sequence and the chunk up to itself); one step = one layer for all 32,768
+    "prefill": dict(desc="config 5 attention: 16 seqs x 2048-token chunks, each token attending its top-2048 "
+                         "rows of a causal window over 300,000 prior tokens (stratified random picks through a "
+                         "shuffled page table of a 2,713,846-token pool), 64 heads",
+                    B=16, H=64, QL=1, ctx=2048, topk=2048, prior=300000, pool_tokens=2713846, prefill=True),
     "long": dict(desc="config 4 (one layer): 5 x 460,000 + 3 x 900,000-token sequences, 64 heads, "
                       "MTP q_len 3, token-balanced sequence / page-range partition over the ranks",
                  B=8, H=64, QL=3, ctx=0, topk=0, lens=[460000] * 5 + [900000] * 3),
 }
+
+
+def load_measured(key: str, fallback: float) -> float:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p)).get(key, fallback))
+    return fallback
 
 
 def load_peaks():
@@ -200,6 +214,8 @@ DEDUP_ROW_BYTES = NV_BYTES + 656    # distinct row read, 656 B row written
 
 
 def kv_bytes_per_step(wl) -> int:
+    if wl.get("prefill"):
+        return wl["B"] * wl["ctx"] * wl["topk"] * NV_BYTES
     if wl.get("dedup"):
         raise ValueError("the dedup workload's bytes depend on its distinct entries (dedup_bytes)")
     if "pool_tokens" in wl:
@@ -622,6 +638,175 @@ def run_append(args, wl, rt, torch, dist, dev, rank, world, local):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+PREFILL_FLOPS_PER_ROW = 64 * 2 * (512 + 512)   # per query token and attended row: QK^T and PV, 64 heads
+
+
+def make_prefill(rt, torch, wl, dev, seed):
+    """Config 5's attention step: a 2.7M-token pool written by the append kernel (N(0,1) latent,
+    1 % of values x20), and for each of the 16 x 2048 new tokens its top-2048 pool rows: one pick
+    per 1/2048 stratum of its causal window (positions below 300,000 + its index + 1), mapped
+    through its sequence's shuffled page table, so the picks are distinct and spread over the
+    window as an indexer's are.  Returns the layer dict decode calls take."""
+    B, T, K, H, prior = wl["B"], wl["ctx"], wl["topk"], wl["H"], wl["prior"]
+    pages_total = wl["pool_tokens"] // 64
+    pool = torch.empty(pages_total, 64, NV_BYTES, dtype=torch.uint8, device=dev)
+    torch.manual_seed(seed)
+    for c in range(0, pages_total * 64, 1 << 20):
+        n = min(1 << 20, pages_total * 64 - c)
+        x = torch.randn(n, 512, device=dev)
+        x = torch.where(torch.rand(n, 512, device=dev) < 0.01, x * 20.0, x)
+        rt.write_nvfp4(x.to(torch.bfloat16), pool, torch.arange(c, c + n, device=dev))
+    g = torch.Generator(device=dev).manual_seed(seed)
+    npages = (prior + T + 63) // 64
+    tables = torch.empty(B * T, 1, K, dtype=torch.int32, device=dev)
+    ar = torch.arange(K, device=dev, dtype=torch.float64)
+    for s_ in range(B):
+        pt = torch.randperm(pages_total, generator=g, device=dev)[:npages]
+        vis = (prior + 1 + torch.arange(T, device=dev)).to(torch.float64)
+        u = torch.rand(T, K, generator=g, device=dev, dtype=torch.float64)
+        pos = torch.minimum(((ar + u) * vis[:, None] / K).long(), vis[:, None].long() - 1)
+        tables[s_ * T:(s_ + 1) * T, 0] = (pt[pos // 64] * 64 + pos % 64).to(torch.int32)
+    q = torch.randn(B * T, 1, H, 576, generator=g, device=dev).to(torch.bfloat16)
+    return dict(pool=pool, tables=tables, q=q, seq=torch.full((B * T,), K, dtype=torch.int32, device=dev),
+                out=torch.empty(B * T, 1, H, 512, dtype=torch.bfloat16, device=dev))
+
+
+def prefill_check(torch, rt, ly, tokens, sm):
+    """Decode outputs of the given query tokens against the exact dequantised attention (fp32)."""
+    worst, ok = 0.0, True
+    for j in tokens:
+        kv = rt.dequant(ly["pool"], ly["tables"][j, 0]).float()
+        qf = ly["q"][j, 0, :, :512].float()
+        tru = torch.softmax(qf @ kv.t() * sm, dim=-1) @ kv
+        o = ly["out"][j, 0].float()
+        worst = max(worst, float((o - tru).norm() / tru.norm()))
+        ok = ok and bool(((o - tru).abs() <= 1e-2 + 2e-2 * tru.abs()).all())
+    return {"fp32_rel_l2_max": round(worst, 5), "fp32_within_tol": ok, "tokens_checked": len(tokens), "passed": ok}
+
+
+def run_prefill(args, wl, rt, torch, dist, dev, rank, world, local):
+    """--workload prefill: config 5's attention step, the fused sparse kernel with one query
+    group per new token (weak scaling: a pool and 16 sequences per rank)."""
+    ly = make_prefill(rt, torch, wl, dev, seed=1 + rank)
+    n_q = ly["q"].shape[0]
+    K = wl["topk"]
+    sm = 1.0 / math.sqrt(576)
+    kvb = kv_bytes_per_step(wl)
+    flops = n_q * K * PREFILL_FLOPS_PER_ROW
+
+    def call(out=None, q=None, tables=None):
+        return rt.mla_decode(ly["q"] if q is None else q, ly["pool"], None, 128, 512, 64,
+                             ly["tables"] if tables is None else tables, ly["seq"], K, sparse_mla_top_k=K,
+                             out=ly["out"] if out is None else out, bmm1_scale=sm, bmm2_scale=1.0)
+
+    call()
+    torch.cuda.synchronize()
+    s_ = torch.cuda.Stream()
+    s_.wait_stream(torch.cuda.current_stream())
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s_):
+        with torch.cuda.graph(gr, stream=s_):
+            call()
+    torch.cuda.current_stream().wait_stream(s_)
+    torch.cuda.synchronize()
+    steps = args.steps if args.steps_given else 20
+    sampler = ClockSampler(local)
+    sampler.start()
+    soak_end = time.perf_counter() + 1.0
+    k = 0
+    while time.perf_counter() < soak_end or k < args.warmup:
+        gr.replay()
+        k += 1
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(steps):
+        gr.replay()
+    ev1.record()
+    ev1.synchronize()
+    t1 = time.perf_counter()
+    if world > 1:
+        dist.barrier()
+    sampler.stop()
+    t_max = torch.tensor([ev0.elapsed_time(ev1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    per_ms = float(t_max.item()) / steps
+    value = kvb * world / (per_ms / 1e3) / 1e9
+
+    # the attention kernel alone (events the library records around it)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(3)]
+    for a, b in kev:
+        rt.set_kernel_events(a, b)
+        call()
+    torch.cuda.synchronize()
+    kernel_ms = sum(a.elapsed_time(b) for a, b in kev) / len(kev)
+
+    # end to end through the public API: q and the top-k tables host->device, the output back,
+    # serial on one stream (each step's copies are several times its decode)
+    q_h = ly["q"].cpu().pin_memory()
+    t_h = ly["tables"].cpu().pin_memory()
+    o_h = torch.empty(ly["out"].shape, dtype=torch.bfloat16).pin_memory()
+    qd, td = torch.empty_like(ly["q"]), torch.empty_like(ly["tables"])
+    e_steps = 3
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e_steps):
+        qd.copy_(q_h, non_blocking=True)
+        td.copy_(t_h, non_blocking=True)
+        call(q=qd, tables=td)
+        o_h.copy_(ly["out"], non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = kvb * world * e_steps / (float(e_ms.item()) / 1e3) / 1e9
+    check = prefill_check(torch, rt, ly, [0, wl["ctx"] - 1, n_q - 1], sm)
+    errors = rt.device_errors(dev)
+    if rank == 0:
+        peak = load_measured("bf16_tflops_sustained", 1400.0)
+        achieved = flops / (kernel_ms / 1e3) / 1e12
+        line = {
+            "metric": METRIC + " (prefill attention step)", "value": round(value, 2), "unit": "GB/s",
+            "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded N(0,1) latent with 1 % x20 quantised by the append kernel; N(0,1) q)",
+            "config": {"workload": wl["desc"], "query_tokens": n_q, "topk": K, "heads": wl["H"],
+                       "pool_rows": wl["pool_tokens"] // 64 * 64,
+                       "l2": f"inputs larger than L2: {kvb / 2**30:.1f} GiB of row reads per step from a "
+                             f"{wl['pool_tokens'] * NV_BYTES / 2**20:.0f} MiB pool",
+                       "parallelism": f"a pool and 16 sequences per rank x{world} (weak scaling)"},
+            "query_tokens_per_s": round(n_q * world / (per_ms / 1e3), 1),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": "measured bf16 sustained",
+                         "flops_per_launch": flops, "kernel_ms": round(kernel_ms, 4),
+                         "kernel": "decode_fp4_kernel<sparse>", "traffic": profile_traffic("prefill"),
+                         "step_frac_in_kernel": round(kernel_ms / per_ms, 3)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": q_h.numel() * 2 + t_h.numel() * 4, "d2h_bytes_per_step": o_h.numel() * 2,
+                    "steps": e_steps},
+            "gpu_launches": steps * 2,
+            "clocks": sampler.summary(t0, t1),
+            "result_check": check,
+            "device_errors": errors,
+        }
+        print(json.dumps(line), flush=True)
+    del gr
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if not check["passed"]:
+        sys.exit("result check failed: a prefill output is outside 2e-2 rel / 1e-2 abs")
 
 
 def run_long(args, wl, rt, torch, dist, dev, rank, world, local):
@@ -1092,13 +1277,16 @@ def check_ranks(torch, rt, dist, wl, L, dev, rank, world, call, sm):
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--workload", default="dense8k", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     args = ap.parse_args()
+    args.steps_given = args.steps is not None
+    if args.steps is None:
+        args.steps = 2000
     wl = WORKLOADS[args.workload]
     if args.warmup < 3:
         args.warmup = 3
@@ -1122,6 +1310,9 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     if "lens" in wl:
         run_long(args, wl, rt, torch, dist, dev, rank, world, local)
+        return
+    if wl.get("prefill"):
+        run_prefill(args, wl, rt, torch, dist, dev, rank, world, local)
         return
     if wl.get("dedup"):
         run_dedup(args, wl, rt, torch, dist, dev, rank, world, local)

@@ -289,6 +289,11 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
           "r"(r[14]), "r"(r[15])
         : "memory");
 }
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};"
+                 ::"r"(taddr), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+                 : "memory");
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -349,6 +354,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst_smem, const void* tmap,
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
         "[%0], [%1, {%2, %3}], [%4];"
         ::"r"(dst_smem), "l"(tmap), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+// TMA row gather (tile::gather4): rows[0..3] of a 2-D tensor map whose box is one row high,
+// starting at column x, written one after another at dst_smem (swizzled as the map says).
+__device__ __forceinline__ void tma_gather4(uint32_t dst_smem, const void* tmap, int x, const int (&rows)[4],
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+        ::"r"(dst_smem), "l"(tmap), "r"(x), "r"(rows[0]), "r"(rows[1]), "r"(rows[2]), "r"(rows[3]), "r"(bar)
         : "memory");
 }
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {

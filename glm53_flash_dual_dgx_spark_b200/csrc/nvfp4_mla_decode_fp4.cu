@@ -19,9 +19,10 @@
 // 32 (w >> 2) .. +32), 8-11 producers, 12 MMA issue, 13 loads.  Per 128-token tile i:
 //   loads    3-slot ring of tiles: codes [2 x 128 rows x 128 B] swizzled + scales [128 x 32 B].
 //            Dense (paged): TMA boxes straight from the pages; pages missing or beyond the
-//            context load as out-of-range boxes (zeros).  Sparse (top-k rows): each lane
-//            copies its rows with 16-byte asynchronous copies straight into the slot layout,
-//            zero-filling masked rows, so everything downstream is shared with the dense path.
+//            context load as out-of-range boxes (zeros).  Sparse (top-k rows): TMA row gathers
+//            (tile::gather4, four rows per instruction) into the same slot layout, so everything
+//            downstream is shared with the dense path; masked rows never reach the output
+//            (probability 0, V written as zeros).
 //   producers  V chunks of 16 tokens -> fp16 [8 d-atoms x 16 tokens x 128 B] (2 buffers).
 //   MMA      QK(i): 16 fp4 MMAs M128 N128 K64 -> S^T; PV(i-1): 8 chunks x 4 fp16 MMAs.
 //   softmax  S^T row t -> x = s * log2(e) * bmm1_scale, masked; the running max of each query
@@ -47,8 +48,6 @@ constexpr int kTile = kDecTile;                   // 128 tokens: QK M
 constexpr int kNQ = kDecRows;                     // 64 query rows: PV N
 constexpr int kChunk = 16;                        // tokens per V chunk = PV K
 constexpr int kChunks = kTile / kChunk;           // 8
-constexpr int kSlots = 3;                         // tile ring depth
-constexpr int kVBufs = 2;                         // V chunk buffers
 // Four warpgroups.  Registers are moved between them at run time (setmaxnreg): the block is
 // launched with 128 per thread; softmax takes 168, producers keep 96, the control group 80.
 constexpr int kSoftmaxWarps = 8;                  // warpgroups 0-1: 2 per TMEM sub-partition, 32 rows each
@@ -63,46 +62,54 @@ static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsProducer + 128 * kRegsCtl == k
               "the register split uses exactly what the block is launched with");
 constexpr float kRescaleLog2 = 8.0f;
 
-// Shared memory map (offsets from a 1024-byte aligned base).
+// Shared memory map (offsets from a 1024-byte aligned base) of a ring of S raw tiles and V
+// V-chunk buffers.  Two shapes are built: S = 3, V = 2 (tiles loaded two ahead; long contexts)
+// and S = 2, V = 4 (the third tile's 36 KB hold two more V chunks, so four chunks are in flight
+// between the producers and the tensor core; splits of at most two tiles, where a third slot
+// would never be loaded).
 constexpr int kCodeBytes = kTile * 256;               // 2 atom columns x [128 rows x 128 B]
 constexpr int kScaleBytes = kTile * 32;               // [128 rows x 32 B]
 constexpr int kSlotBytes = kCodeBytes + kScaleBytes;  // 36864
+constexpr int kVtBytes = 8 * kChunk * 128;            // one V chunk: [8 d-atoms x 16 tokens x 128 B] fp16
 constexpr int SM_STAGE = 0;
-constexpr int SM_QB = SM_STAGE + kSlots * kSlotBytes;     // Q terms: 2 passes x 2 atom columns x [128 x 128 B]
-constexpr int SM_VT = SM_QB + 2 * kCodeBytes;             // kVBufs x [8 d-atoms x 16 tokens x 128 B] fp16
-constexpr int kVtBytes = 8 * kChunk * 128;
-constexpr int SM_PT = SM_VT + kVBufs * kVtBytes;          // [128 tokens x 128 B] fp16 P^T
-constexpr int SM_M = SM_PT + kTile * 128;                 // 64 f32: running row max (log2 units)
-constexpr int SM_ALPHA = SM_M + 256;                      // 64 f32: rescale factors / epilogue 1/l
-constexpr int SM_QS = SM_ALPHA + 256;                     // 64 f32: log2e * bmm1_scale * 2^e_row
-constexpr int SM_LIM = SM_QS + 256;                       // 64 i32: visible positions < lim
-constexpr int SM_LSUM = SM_LIM + 256;                     // 64 f32: row sums
-constexpr int SM_RED = SM_LSUM + 256;                     // 4 sub-partitions x 64 f32
-constexpr int SM_ROWOFF = SM_RED + 4 * 64 * 4;            // 64 i64: output row offsets
-constexpr int SM_FLAGS = SM_ROWOFF + 64 * 8;              // [0] TMEM base, [1] abort
-constexpr int SM_TMASK = SM_FLAGS + 16;                   // kSlots x 4 words: tile rows that are valid
-constexpr int SM_BARS = SM_TMASK + kSlots * 16;
-enum {
-    B_FULL = 0,                    // [kSlots] raw tile landed (TMA bytes / cp.async arrivals)
-    B_FREE = B_FULL + kSlots,      // [kSlots] producers finished reading the slot
-    B_QKD = B_FREE + kSlots,       // [kSlots] QK finished reading the slot
-    B_SFA_FULL = B_QKD + kSlots,   // [2] pool scales of a tile written to TMEM
-    B_S_FULL = B_SFA_FULL + 2,     // S^T complete in TMEM
-    B_S_FREE,                      // softmax has S^T in registers
-    B_P_FULL,                      // P^T complete in shared memory
-    B_PV_DONE,                     // PV of a tile complete (O^T stable, P^T free)
-    B_V_FULL,                      // [kVBufs] V chunk written
-    B_V_EMPTY = B_V_FULL + kVBufs, // [kVBufs] PV finished reading the V chunk
-    B_Q = B_V_EMPTY + kVBufs,      // prepared Q landed (set-up)
-    B_DRAIN,                       // every MMA of the CTA complete (before TMEM is freed)
-    kNumBars
+constexpr int kMaxIdx = 768;                          // staged page ids / top-k rows of the split
+constexpr int kIdxTiles = kMaxIdx / kTile;            // sparse: a window of 6 tiles' rows, refilled ahead
+template <int S, int V>
+struct DecCfg {
+    static constexpr int kSlots = S;                                 // tile ring depth
+    static constexpr int kVBufs = V;                                 // V chunk buffers
+    static constexpr int SM_QB = SM_STAGE + S * kSlotBytes;          // Q terms: 2 passes x 2 atom columns x [128 x 128 B]
+    static constexpr int SM_VT = SM_QB + 2 * kCodeBytes;             // V x [8 d-atoms x 16 tokens x 128 B] fp16
+    static constexpr int SM_PT = SM_VT + V * kVtBytes;               // [128 tokens x 128 B] fp16 P^T
+    static constexpr int SM_M = SM_PT + kTile * 128;                 // 64 f32: running row max (log2 units)
+    static constexpr int SM_ALPHA = SM_M + 256;                      // 64 f32: rescale factors / epilogue 1/l
+    static constexpr int SM_QS = SM_ALPHA + 256;                     // 64 f32: log2e * bmm1_scale * 2^e_row
+    static constexpr int SM_LIM = SM_QS + 256;                       // 64 i32: visible positions < lim
+    static constexpr int SM_LSUM = SM_LIM + 256;                     // 64 f32: row sums
+    static constexpr int SM_RED = SM_LSUM + 256;                     // 4 sub-partitions x 64 f32
+    static constexpr int SM_ROWOFF = SM_RED + 4 * 64 * 4;            // 64 i64: output row offsets
+    static constexpr int SM_FLAGS = SM_ROWOFF + 64 * 8;              // [0] TMEM base, [1] abort
+    static constexpr int SM_TMASK = SM_FLAGS + 16;                   // S x 4 words: tile rows that are valid
+    static constexpr int SM_BARS = SM_TMASK + S * 16;
+    static constexpr int B_FULL = 0;                    // [S] raw tile landed (TMA bytes / cp.async arrivals)
+    static constexpr int B_FREE = B_FULL + S;           // [S] producers finished reading the slot
+    static constexpr int B_QKD = B_FREE + S;            // [S] QK finished reading the slot
+    static constexpr int B_SFA_FULL = B_QKD + S;        // [2] pool scales of a tile written to TMEM
+    static constexpr int B_S_FULL = B_SFA_FULL + 2;     // S^T complete in TMEM
+    static constexpr int B_S_FREE = B_S_FULL + 1;       // softmax has S^T in registers
+    static constexpr int B_P_FULL = B_S_FREE + 1;       // P^T complete in shared memory
+    static constexpr int B_PV_DONE = B_P_FULL + 1;      // PV of a tile complete (O^T stable, P^T free)
+    static constexpr int B_V_FULL = B_PV_DONE + 1;      // [V] V chunk written
+    static constexpr int B_V_EMPTY = B_V_FULL + V;      // [V] PV finished reading the V chunk
+    static constexpr int B_Q = B_V_EMPTY + V;           // prepared Q landed (set-up)
+    static constexpr int B_DRAIN = B_Q + 1;             // every MMA of the CTA complete (before TMEM is freed)
+    static constexpr int kNumBars = B_DRAIN + 1;
+    static constexpr int SM_IDX = SM_BARS + ((kNumBars * 8 + 15) / 16) * 16;
+    static constexpr int SM_END = SM_IDX + kMaxIdx * 4;
+    static constexpr int kSmemBytes = SM_END + 1024;                 // slack to align the base
+    static_assert(kSmemBytes <= 232448, "shared memory budget");
+    static_assert(SM_VT >= kNQ * kLatent * 4, "epilogue staging fits below the V buffers");
 };
-constexpr int SM_IDX = SM_BARS + ((kNumBars * 8 + 15) / 16) * 16;
-constexpr int kMaxIdx = 768;                              // staged page ids of the split
-constexpr int SM_END = SM_IDX + kMaxIdx * 4;
-constexpr int kSmemBytes = SM_END + 1024;                 // slack to align the base
-static_assert(kSmemBytes <= 232448, "shared memory budget");
-static_assert(SM_VT >= kNQ * kLatent * 4, "epilogue staging fits below the V buffers");
 static_assert(kQImageBytes == 2 * kCodeBytes + 2 * 4096 + 256, "prepared-Q image layout");
 
 // Tensor memory columns (all 128 lanes).
@@ -277,7 +284,8 @@ template <bool kSparse>
 __device__ __forceinline__ int64_t token_row(const Fp4Params& p, const int* sidx, bool staged, int idx_base,
                                              int b, int pos, bool report) {
     if constexpr (kSparse) {
-        const int idx = staged ? sidx[pos - idx_base] : __ldg(p.tables + b * p.tables_stride + pos);
+        // sparse rows are staged as a window of kIdxTiles tiles (tile j at j % kIdxTiles)
+        const int idx = staged ? sidx[(pos - idx_base) % kMaxIdx] : __ldg(p.tables + b * p.tables_stride + pos);
         if (idx < 0 || idx >= p.pool_rows) {
             if (report && idx != -1) set_error(p.err, NVFP4KV_DEVERR_BAD_INDEX);
             return -1;
@@ -290,65 +298,52 @@ __device__ __forceinline__ int64_t token_row(const Fp4Params& p, const int* sidx
     }
 }
 
-// Sparse: the rows of tile `tile_start` (lane l: rows l + 32k) straight into the ring slot at
-// `slot_base` with 16-byte asynchronous copies: codes into the 128-byte swizzled K-major
-// atoms, scales at 32 B per row.  Masked rows (-1 padding, out-of-range entries, positions
-// past `end`) are zero-filled without a read.  Every lane's copies arrive on `bar_full`
-// once landed; lane 0 then writes the slot's valid-row mask and makes the barrier's one
-// expected arrival, so the phase completes when the mask is written and every row is in.
-__device__ __forceinline__ void load_rows_async(const Fp4Params& p, uint32_t slot_base, uint32_t bar_full,
-                                                uint32_t* slot_mask, const int* sidx, bool staged,
-                                                int idx_base, int b, int tile_start, int end, int lane) {
+// Sparse: the rows of tile `tile_start` into the ring slot at `slot_base` by TMA row gathers
+// (tile::gather4: four arbitrary pool rows per instruction, the box one row high): lane l
+// fetches rows 4l .. 4l + 3 of the tile as three gathers, the two 128-byte halves of their
+// codes (written 128-byte swizzled, the layout the dense path's tile boxes produce) and their
+// 32 scale bytes.  The TMA unit keeps the whole tile in flight, where per-thread 16-byte
+// copies were bound by the SM's issue and request rate.  A masked row (-1 padding, an
+// out-of-range entry, a position past `end`) is fetched from pool row 0: its bit stays clear
+// in the slot's valid-row mask, the softmax gives it probability 0 and the producers write
+// its V as zeros, so nothing of that row reaches the output.  Lane 0 writes the mask and arms
+// the barrier with the tile's bytes before any gather is issued.
+__device__ __forceinline__ void load_rows_gather4(const Fp4Params& p, const void* tm_codes, const void* tm_scales,
+                                                  uint32_t slot_base, uint32_t bar_full, uint32_t* slot_mask,
+                                                  const int* sidx, int idx_base, int b, int tile_start, int end,
+                                                  int lane) {
+    int rows[4];
     uint32_t live = 0;
-    if (staged) {
-        // the tile's 128 x 18 16-byte chunks numbered row-major; one instruction copies 32
-        // consecutive chunks (about two whole rows), so each row costs a few wide requests
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int pos = tile_start + 32 * k + lane;
-            const int64_t row = pos < end ? token_row<true>(p, sidx, true, idx_base, b, pos, true) : -1;
-            live |= static_cast<uint32_t>(row >= 0) << k;
-        }
-#pragma unroll 4
-        for (int i = 0; i < kTile * 18 / 32; ++i) {
-            const int c = 32 * i + lane;
-            const int r = c / 18, k = c - 18 * r;
-            const int pos = tile_start + r;
-            const int idx = pos < end ? sidx[pos - idx_base] : -1;
-            const bool ok = idx >= 0 && idx < p.pool_rows;
-            const uint8_t* src = p.pool + static_cast<int64_t>(ok ? idx : 0) * kRowBytes + 16 * k;
-            const uint32_t dst = k < 16 ? slot_base + (k >> 3) * 16384 + (r >> 3) * 1024 + (r & 7) * 128 +
-                                              (((k & 7) ^ (r & 7)) << 4)
-                                        : slot_base + kCodeBytes + r * 32 + 16 * (k - 16);
-            cp_async16_zfill(dst, src, ok ? 16u : 0u);
-        }
-    } else {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int r = 32 * k + lane;
-            const int pos = tile_start + r;
-            const int64_t row = pos < end ? token_row<true>(p, sidx, staged, idx_base, b, pos, true) : -1;
-            const bool ok = row >= 0;
-            live |= static_cast<uint32_t>(ok) << k;
-            const uint8_t* src = p.pool + (ok ? row : 0) * kRowBytes;
-            const uint32_t nbytes = ok ? 16u : 0u;
-            const uint32_t drow = slot_base + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-            for (int c = 0; c < 16; ++c)
-                cp_async16_zfill(drow + (c >> 3) * 16384 + (((c & 7) ^ (r & 7)) << 4), src + 16 * c, nbytes);
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-                cp_async16_zfill(slot_base + kCodeBytes + r * 32 + 16 * h, src + 256 + 16 * h, nbytes);
-        }
+    for (int j = 0; j < 4; ++j) {
+        const int pos = tile_start + 4 * lane + j;
+        const int64_t row = pos < end ? token_row<true>(p, sidx, true, idx_base, b, pos, true) : -1;
+        live |= static_cast<uint32_t>(row >= 0) << j;
+        rows[j] = row >= 0 ? static_cast<int>(row) : 0;
     }
-    cp_async_mbar_arrive(bar_full);
+    // lane l holds rows 4l .. 4l+3.  bits[j] bit l: row 4l + j is live.  Mask word k covers rows
+    // 32k .. 32k+31, i.e. lanes 8k .. 8k+7: row 32k + 4m + j is bit 4m + j of word k.
+    uint32_t bits[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const uint32_t w = __ballot_sync(0xFFFFFFFFu, (live >> k) & 1u);
-        if (lane == 0) slot_mask[k] = w;
+    for (int j = 0; j < 4; ++j) bits[j] = __ballot_sync(0xFFFFFFFFu, (live >> j) & 1u);
+    if (lane == 0) {   // the thread that arms the barrier writes the whole mask
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            uint32_t w = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int m = 0; m < 8; ++m) w |= ((bits[j] >> (8 * k + m)) & 1u) << (4 * m + j);
+            slot_mask[k] = w;
+        }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(bar_full);
+    if (lane == 0) mbar_arrive_expect_tx(bar_full, kSlotBytes);
+    __syncwarp();
+    const int r0 = 4 * lane;
+    tma_gather4(slot_base + r0 * 128, tm_codes, 0, rows, bar_full);
+    tma_gather4(slot_base + 16384 + r0 * 128, tm_codes, 128, rows, bar_full);
+    tma_gather4(slot_base + kCodeBytes + r0 * 32, tm_scales, 256, rows, bar_full);
 }
 
 // Pool scales of the tile in `slot` -> TMEM scale-factor columns `col` of this warp's
@@ -367,6 +362,17 @@ __device__ __forceinline__ void scales_to_tmem(const uint8_t* scales, uint32_t t
             rr[12 + q4] = w.w;
         }
         tmem_st16(taddr + 16 * half, rr);
+    }
+    tmem_wait_st();
+}
+
+// scales_to_tmem four columns at a time (same layout), for call sites where registers are
+// scarce: column 4kk+q of lane r holds word kk of token 32q + r's 32 scale bytes.
+__device__ __forceinline__ void scales_to_tmem_narrow(const uint8_t* scales, uint32_t taddr, int lane) {
+#pragma unroll 1
+    for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(scales + lane * 32 + 4 * kk);
+        tmem_st4(taddr + 4 * kk, w[0], w[32 * 8], w[64 * 8], w[96 * 8]);
     }
     tmem_wait_st();
 }
@@ -445,11 +451,20 @@ __device__ __forceinline__ void probs32(const float (&sraw)[32], const float* qs
 }
 
 // kSparse: the table holds pool rows (top-k, -1 padded) instead of page ids; the tensor maps
-// are unused.
-template <bool kSparse>
+// have one-row boxes for the row gathers.
+template <bool kSparse, int kRing, int kVBuf>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ CUtensorMap tm_codes,
                   const __grid_constant__ CUtensorMap tm_scales) {
+    using C = DecCfg<kRing, kVBuf>;
+    constexpr int kSlots = C::kSlots, kVBufs = C::kVBufs;
+    constexpr int SM_QB = C::SM_QB, SM_VT = C::SM_VT, SM_PT = C::SM_PT, SM_M = C::SM_M, SM_ALPHA = C::SM_ALPHA;
+    constexpr int SM_QS = C::SM_QS, SM_LIM = C::SM_LIM, SM_LSUM = C::SM_LSUM, SM_RED = C::SM_RED;
+    constexpr int SM_ROWOFF = C::SM_ROWOFF, SM_FLAGS = C::SM_FLAGS, SM_TMASK = C::SM_TMASK, SM_BARS = C::SM_BARS;
+    constexpr int SM_IDX = C::SM_IDX;
+    constexpr int B_FULL = C::B_FULL, B_FREE = C::B_FREE, B_QKD = C::B_QKD, B_SFA_FULL = C::B_SFA_FULL;
+    constexpr int B_S_FULL = C::B_S_FULL, B_S_FREE = C::B_S_FREE, B_P_FULL = C::B_P_FULL, B_PV_DONE = C::B_PV_DONE;
+    constexpr int B_V_FULL = C::B_V_FULL, B_V_EMPTY = C::B_V_EMPTY, B_Q = C::B_Q, B_DRAIN = C::B_DRAIN;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -513,9 +528,11 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
     // page ids (dense) / pool rows (sparse) of this split
     const int idx_base = kSparse ? start : start >> p.page_shift;
     const int idx_count = end <= start ? 0 : kSparse ? end - start : ((end - 1) >> p.page_shift) - idx_base + 1;
-    const bool staged = idx_count <= kMaxIdx;
+    // dense: the split's page ids when they fit; sparse: always, as a window of the first
+    // kIdxTiles tiles' rows that the load warp refills ahead of its copies
+    const bool staged = kSparse || idx_count <= kMaxIdx;
     if (staged)
-        for (int k = threadIdx.x; k < idx_count; k += kThreads)
+        for (int k = threadIdx.x; k < min(idx_count, kMaxIdx); k += kThreads)
             sidx[k] = __ldg(p.tables + b * p.tables_stride + idx_base + k);
     tc_fence_before();
     __syncthreads();
@@ -539,7 +556,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             bulk_copy_g2s(sbase + SM_PT, img + 2 * kCodeBytes, 2 * 4096, bar(B_Q));
             bulk_copy_g2s(sbase + SM_QS, img + 2 * kCodeBytes + 2 * 4096, 256, bar(B_Q));
         };
-        if (!kSparse && lane == 0) {
+        if (lane == 0) {
             tma_prefetch_desc(&tm_codes);
             tma_prefetch_desc(&tm_scales);
         }
@@ -547,12 +564,20 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             // tile j -> slot j % kSlots once QK(j - kSlots) and the producers are done with it
             int issued = 0;   // tiles issued; tile j completes phase j / kSlots of its slot
             for (int j = 0; j < kSlots && j < n_tiles; ++j) {
-                load_rows_async(p, sbase + SM_STAGE + j * kSlotBytes, bar(B_FULL + j), tmask + 4 * j, sidx,
-                                staged, idx_base, b, start + j * kTile, end, lane);
+                load_rows_gather4(p, &tm_codes, &tm_scales, sbase + SM_STAGE + j * kSlotBytes, bar(B_FULL + j),
+                                  tmask + 4 * j, sidx, idx_base, b, start + j * kTile, end, lane);
                 issued = j + 1;
                 if (j == 0 && lane == 0) load_q();
             }
             if (n_tiles == 0 && lane == 0) load_q();
+            // Splits longer than the index window: after tile t is issued, the rows of tile
+            // t + kSlots are loaded into registers (window slot (t + kSlots) % kIdxTiles, whose
+            // tile t + kSlots - kIdxTiles was issued long before) and stored before the next
+            // issue, so no copy waits on a table load.
+            static_assert(2 * kSlots <= kIdxTiles, "index window covers the refill distance");
+            const bool refill = idx_count > kMaxIdx;
+            int pend[4] = {-1, -1, -1, -1};
+            int pend_tile = -1;
 #pragma unroll 1
             for (int i = 0; i + kSlots < n_tiles; ++i) {
                 const int slot = i % kSlots;
@@ -561,10 +586,26 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
                 const bool d = mbar_wait(bar(B_QKD + slot), sph, abort_flag, p.err);
                 // after an abort nothing more is issued (the drain below waits for what was)
                 if (!__all_sync(0xFFFFFFFFu, f && d && !*abort_flag)) break;
+                if (pend_tile >= 0) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) sidx[(pend_tile % kIdxTiles) * kTile + 32 * k + lane] = pend[k];
+                    __syncwarp();
+                }
                 fence_proxy_async_smem();
-                load_rows_async(p, sbase + SM_STAGE + slot * kSlotBytes, bar(B_FULL + slot), tmask + 4 * slot,
-                                sidx, staged, idx_base, b, start + (i + kSlots) * kTile, end, lane);
-                issued = i + kSlots + 1;
+                const int t = i + kSlots;
+                load_rows_gather4(p, &tm_codes, &tm_scales, sbase + SM_STAGE + slot * kSlotBytes,
+                                  bar(B_FULL + slot), tmask + 4 * slot, sidx, idx_base, b, start + t * kTile, end,
+                                  lane);
+                issued = t + 1;
+                pend_tile = -1;
+                if (refill && t + kSlots >= kIdxTiles && t + kSlots < n_tiles) {
+                    pend_tile = t + kSlots;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int pos = start + pend_tile * kTile + 32 * k + lane;
+                        pend[k] = pos < end ? __ldg(p.tables + b * p.tables_stride + pos) : -1;
+                    }
+                }
             }
             for (int j = issued > kSlots ? issued - kSlots : 0; j < issued; ++j)
                 mbar_drain_wait(bar(B_FULL + j % kSlots), (j / kSlots) & 1);
@@ -611,7 +652,6 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
                 mbar_wait(bar(B_SFA_FULL + fb), (i >> 1) & 1, abort_flag, p.err);
                 if (i > 0) mbar_wait(bar(B_S_FREE), (i - 1) & 1, abort_flag, p.err);
                 tc_fence_after();
-                if constexpr (kSparse) fence_proxy_async_smem();   // cp.async rows -> tensor core
                 const uint64_t da0 = smem_desc_sw128(sbase + SM_STAGE + slot * kSlotBytes, 16, 1024);
                 const uint32_t sfa = tmem + kTSFA + 32 * fb, sfb = tmem + kTSFB;
                 if (elect_one()) {
@@ -693,6 +733,14 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
                         for (int k = 0; k < 4; ++k) hv[it][4 * w + k] = hmul2_u32(t4[k], sv);
                     }
                 }
+                // a masked row (padding, a bad entry, a missing page, past the context) may hold
+                // anything, even NaN scales: its V is written as zeros (its probability is 0)
+                if (!((tmask[4 * slot + (tok >> 5)] >> (tok & 31)) & 1u)) {
+#pragma unroll
+                    for (int it = 0; it < 2; ++it)
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) hv[it][k] = 0u;
+                }
                 if (u >= kVBufs) mbar_wait(bar(B_V_EMPTY + vb), ((u / kVBufs) - 1) & 1, abort_flag, p.err);
                 uint8_t* vt = smem + SM_VT + vb * kVtBytes + tq * 128;
 #pragma unroll
@@ -766,11 +814,16 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             mbar_wait(bar(B_S_FULL), i & 1, abort_flag, p.err);
             tc_fence_after();
             // pool scales of tile i+1 -> its TMEM slot (QK(i-1), the slot's last reader, is
-            // complete: S_FULL(i) tracks every earlier MMA); the ring loads tiles two ahead
-            if (hh == 0 && i + 1 < n_tiles) {
-                const int slot1 = (i + 1) % kSlots;
-                mbar_wait(bar(B_FULL + slot1), ((i + 1) / kSlots) & 1, abort_flag, p.err);
-                scales_to_tmem(smem + SM_STAGE + slot1 * kSlotBytes + kCodeBytes,
+            // complete: S_FULL(i) tracks every earlier MMA).  In a long split the ring loads
+            // tiles two ahead, so tile i+1 has landed and its scales go now: QK(i+1) runs while
+            // P(i) is computed.  Short sparse splits (one or two tiles, the two-slot ring) start
+            // with both tiles' row gathers in flight: there they go after P(i), which must not
+            // wait for tile i+1 to land.
+            const bool next_tile = hh == 0 && i + 1 < n_tiles;
+            const bool early = next_tile && !(kSparse && kSlots == 2);
+            if (early) {
+                mbar_wait(bar(B_FULL + (i + 1) % kSlots), ((i + 1) / kSlots) & 1, abort_flag, p.err);
+                scales_to_tmem(smem + SM_STAGE + ((i + 1) % kSlots) * kSlotBytes + kCodeBytes,
                                tmem + kTSFA + 32 * ((i + 1) & 1) + lane_base, lane);
                 tc_fence_before();
                 __syncwarp();
@@ -898,6 +951,14 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(B_P_FULL));
+            if (next_tile && !early) {
+                mbar_wait(bar(B_FULL + (i + 1) % kSlots), ((i + 1) / kSlots) & 1, abort_flag, p.err);
+                scales_to_tmem_narrow(smem + SM_STAGE + ((i + 1) % kSlots) * kSlotBytes + kCodeBytes,
+                               tmem + kTSFA + 32 * ((i + 1) & 1) + lane_base, lane);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(B_SFA_FULL + ((i + 1) & 1)));
+            }
         }
 
         // ---- epilogue
@@ -1012,18 +1073,40 @@ int make_pool_map(CUtensorMap* m, const uint8_t* pool, int64_t pool_rows, uint32
     return NVFP4KV_OK;
 }
 
-template <bool kSparse>
+template <bool kSparse, int kRing, int kVBuf>
 int ensure_fp4_smem_attr() {
     static int done[64] = {0};
+    constexpr int bytes = DecCfg<kRing, kVBuf>::kSmemBytes;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaGetDevice failed");
     if (dev >= 0 && dev < 64 && done[dev]) return NVFP4KV_OK;
-    const cudaError_t e = cudaFuncSetAttribute(decode_fp4_kernel<kSparse>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    const cudaError_t e = cudaFuncSetAttribute(decode_fp4_kernel<kSparse, kRing, kVBuf>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess)
-        return fail(NVFP4KV_ECUDA, "cudaFuncSetAttribute(max dynamic smem %d): %s", kSmemBytes, cudaGetErrorString(e));
+        return fail(NVFP4KV_ECUDA, "cudaFuncSetAttribute(max dynamic smem %d): %s", bytes, cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) done[dev] = 1;
     return NVFP4KV_OK;
+}
+
+// The attention launch for one kernel shape (a programmatic dependent of the Q preparation:
+// its set-up overlaps that kernel's tail).
+template <bool kSparse, int kRing, int kVBuf>
+int launch_attention(const Fp4Params& p, const CUtensorMap& tm_codes, const CUtensorMap& tm_scales, dim3 grid,
+                     cudaStream_t st) {
+    int rc;
+    if ((rc = ensure_fp4_smem_attr<kSparse, kRing, kVBuf>()) != NVFP4KV_OK) return rc;
+    const cudaError_t le = launch_dependent(decode_fp4_kernel<kSparse, kRing, kVBuf>, grid, dim3(kThreads),
+                                            DecCfg<kRing, kVBuf>::kSmemBytes, st, p, tm_codes, tm_scales);
+    if (le != cudaSuccess)
+        return fail(NVFP4KV_ECUDA, "nvfp4kv_mla_decode: attention launch failed: %s", cudaGetErrorString(le));
+    return check_launch(kSparse ? "nvfp4kv_mla_decode (fp4 sparse)" : "nvfp4kv_mla_decode (fp4 dense)");
+}
+
+// Ring shape of a call: splits of at most two tiles never load a third ring slot, so its
+// space goes to two more V-chunk buffers.
+bool short_ring(const DecodePlan& pl) {
+    const int longest = (pl.tiles_total + pl.splits - 1) / pl.splits;
+    return longest <= 2;
 }
 
 }  // namespace
@@ -1036,16 +1119,14 @@ int launch_decode_fp4(const DecodeArgs& a, const DecodePlan& pl, cudaStream_t st
         return fail(NVFP4KV_EWORKSPACE, "mla_decode: no 16-byte aligned workspace for the prepared Q");
     if (a.pool_rows > 0x7FFFFFFFll)
         return fail(NVFP4KV_EINVAL, "mla_decode: pool_rows %lld beyond 2^31 - 1", static_cast<long long>(a.pool_rows));
-    const int box_rows = sparse ? 0 : (a.page_size < kTile ? a.page_size : kTile);
+    // dense: boxes of up to a page of rows; sparse: one-row boxes for the row gathers
+    const int box_rows = sparse ? 1 : (a.page_size < kTile ? a.page_size : kTile);
     CUtensorMap tm_codes{}, tm_scales{};
     int rc;
-    if (!sparse) {
-        if ((rc = make_pool_map(&tm_codes, a.pool, a.pool_rows, 128, box_rows, CU_TENSOR_MAP_SWIZZLE_128B)) != NVFP4KV_OK)
-            return rc;
-        if ((rc = make_pool_map(&tm_scales, a.pool, a.pool_rows, 32, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE)) != NVFP4KV_OK)
-            return rc;
-    }
-    if ((rc = sparse ? ensure_fp4_smem_attr<true>() : ensure_fp4_smem_attr<false>()) != NVFP4KV_OK) return rc;
+    if ((rc = make_pool_map(&tm_codes, a.pool, a.pool_rows, 128, box_rows, CU_TENSOR_MAP_SWIZZLE_128B)) != NVFP4KV_OK)
+        return rc;
+    if ((rc = make_pool_map(&tm_scales, a.pool, a.pool_rows, 32, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE)) != NVFP4KV_OK)
+        return rc;
     QPrepParams qp{};
     qp.q = static_cast<const __nv_bfloat16*>(a.q);
     qp.q_sb = a.q_sb; qp.q_sq = a.q_sq; qp.q_sh = a.q_sh;
@@ -1075,15 +1156,12 @@ int launch_decode_fp4(const DecodeArgs& a, const DecodePlan& pl, cudaStream_t st
     cudaEvent_t ev0, ev1;
     take_kernel_events(&ev0, &ev1);
     if (ev0 && cudaEventRecord(ev0, st) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaEventRecord failed");
-    // a programmatic dependent of the Q preparation: set-up overlaps that kernel's tail
-    const cudaError_t le =
-        sparse ? launch_dependent(decode_fp4_kernel<true>, grid, dim3(kThreads), kSmemBytes, st, p, tm_codes, tm_scales)
-               : launch_dependent(decode_fp4_kernel<false>, grid, dim3(kThreads), kSmemBytes, st, p, tm_codes,
-                                  tm_scales);
-    if (le != cudaSuccess)
-        return fail(NVFP4KV_ECUDA, "nvfp4kv_mla_decode: attention launch failed: %s", cudaGetErrorString(le));
-    if ((rc = check_launch(sparse ? "nvfp4kv_mla_decode (fp4 sparse)" : "nvfp4kv_mla_decode (fp4 dense)")) != NVFP4KV_OK)
-        return rc;
+    const bool shrt = short_ring(pl);
+    rc = sparse ? (shrt ? launch_attention<true, 2, 4>(p, tm_codes, tm_scales, grid, st)
+                        : launch_attention<true, 3, 2>(p, tm_codes, tm_scales, grid, st))
+                : (shrt ? launch_attention<false, 2, 4>(p, tm_codes, tm_scales, grid, st)
+                        : launch_attention<false, 3, 2>(p, tm_codes, tm_scales, grid, st));
+    if (rc != NVFP4KV_OK) return rc;
     if (ev1 && cudaEventRecord(ev1, st) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaEventRecord failed");
     return NVFP4KV_OK;
 }

@@ -1,6 +1,6 @@
 """CPU: the benchmark's measurement contract.
 
-The workloads carry BASELINE.json's shapes, the algorithmic bytes per step follow the metric's
+The workloads carry the benchmark configurations' shapes, the algorithmic bytes per step follow the metric's
 definition (288 B per attended token row per query group; 1320 B per appended token), the ncu
 traffic figures the bench reports are the ones committed in profiles/traffic.json, and the reference
 arm (the CPU oracle port, runnable here) prints the one JSON line the driver parses.

@@ -187,6 +187,33 @@ def test_sparse_many_tiles_per_split(rt):
     check(out, ref, "sparse many tiles")
 
 
+def test_sparse_prefill_tokens_one_split_each(rt):
+    """A prefill step through the sparse path: 160 query tokens of one sequence, each with its
+    own top-2048 rows from a causal window (a window grows by one row per token), so every
+    query group is its own CTA (no split) with 16 tiles, and its 2048 row ids stream through
+    the 768-entry window the load warp refills ahead of its copies.  Eight tokens are checked
+    against the oracle."""
+    pool_t, pool = make_pool(320, seed=31)
+    R = 320 * 64
+    g = torch.Generator().manual_seed(32)
+    T, topk, prior = 160, 2048, 16000
+    idx = torch.empty(T, topk, dtype=torch.int32)
+    for i in range(T):
+        idx[i] = torch.randperm(prior + i + 1, generator=g)[:topk].to(torch.int32)
+    perm = torch.randperm(R, generator=g).to(torch.int32)       # positions -> shuffled pool rows
+    idx = perm[idx.long()]
+    sl = torch.full((T,), topk, dtype=torch.int32)
+    sl[5] = 2000                                                  # one ragged count
+    q = torch.randn(T, 1, 64, 576, generator=g).to(torch.bfloat16)
+    out = rt.mla_decode(q.cuda(), pool_t, None, 128, 512, 64, idx.view(T, 1, topk).cuda(), sl.cuda(), topk,
+                        sparse_mla_top_k=topk, bmm1_scale=SM)
+    pick = [0, 5, 37, 64, 99, 128, 150, 159]
+    ref = O.mla_decode(q[pick].float(), pool, idx[pick].view(len(pick), 1, topk).numpy(), sl[pick].numpy(),
+                       sparse=True, bmm1_scale=SM)
+    check(out[pick], ref, "sparse prefill tokens")
+    assert rt.device_errors() == 0
+
+
 def test_sparse_peaked_scores(rt):
     out, ref = run_sparse(rt, 8, 64, 2048, [2048] * 4 + [1500] * 4, qscale=8.0, seed=11)
     check(out, ref, "sparse peaked")
