@@ -2,25 +2,30 @@
 """Benchmark of the NVFP4 paged KV-cache read path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
-                    [--workload dense8k|dense128k|sparse|long|append|dedup]
+                    [--workload sparse|dense8k|dense128k|long|prefill|append|dedup]
                     [--impl ours|reference]
 
-Default workload = BASELINE config 2: dense MLA decode over the 288-byte NVFP4 paged pool,
-batch 16 sequences x 8192 tokens, 64 query heads, qk 576 / v 512, page 64, page tables from
-randperm, q and latent ~N(0,1) bf16 (synthetic, seeded).  One step = one fused
-gather + dequant + MLA decode call (decode kernel + split combine) over the batch for one
-layer; steps rotate over enough layer pools that the data read per cycle exceeds the 126 MB
-L2 (8 x 37.7 MB for config 2), so timed steps read the KV bytes from HBM.
+Default workload = configuration 3, the sparse (indexer) decode the metric is quoted on at
+1/2/4/8 GPUs: batch 16 sequences of 128K tokens on shuffled pages of the 288-byte NVFP4 pool,
+64 query heads, qk 576 / v 512, each sequence's top-2048 rows drawn without replacement
+(synthetic, seeded).  One step = one fused gather + dequant + MLA decode call (Q preparation,
+attention, split combine) over the batch for one layer; steps rotate over 32 layers' top-k
+sets, whose rows (32 x 9.4 MB) exceed the 126 MB L2, so timed steps read the KV rows from HBM.
+dense8k is configuration 2 (batch 16 x 8192 tokens, page tables from randperm).
 
-value  = KV bytes read (288 B per attended token row) per second, whole job (all ranks),
-         device-timed with CUDA events over exactly K steps replayed from CUDA graphs.
+value  = KV bytes read (288 B per attended token row per query group) per second, whole job
+         (all ranks), device-timed with CUDA events over exactly K steps replayed from CUDA
+         graphs.
 e2e    = the same metric through the public API (glm53_nvfp4_runtime.mla_decode), eager,
-         with the per-step q / page-table / seq_lens host->device copies and the output
+         with the per-step q / table / seq_lens host->device copies and the output
          device->host copy (pinned buffers) inside the timed region; the copies of the next
          and previous steps overlap the decode (copy streams, double buffers), as in a
          serving loop; the one-stream serial figure is reported as e2e.serial_value.
+gpu_reference = the reference's own read path on the same GPU (its Triton gather into 656 B
+         rows, then a stock consumer of those rows), N = 1.
 Multi-GPU (torchrun): each rank owns its own 16 sequences and their pages (weak scaling);
-NCCL is used after the timed loop only, to gather the outputs and the max time.
+NCCL is used after the timed loop only: the max time, and one all-gather of the outputs that
+rank 0 checks against its own decode of every other rank's layer.
 """
 from __future__ import annotations
 
@@ -1279,7 +1284,7 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--workload", default="dense8k", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="sparse", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
