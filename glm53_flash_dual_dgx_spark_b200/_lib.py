@@ -52,6 +52,14 @@ SIGNATURES = {
     "nvfp4kv_mla_decode_plan": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
     "nvfp4kv_set_kernel_events": (_I, [_P, _P]),
     "nvfp4kv_selftest_bounded_wait": (_I, [_P, _P]),
+    "nvfp4kv_append_rope": (_I, [_P, _I64, _I64, _P, _I64, _P, _I, _P, _P]),
+    "nvfp4kv_gather_ds656_rope": (_I, [_P, _P, _I64, _P, _I64, _P, _P]),
+    "nvfp4kv_mla_decode_rope": (_I, [_P, _I64, _I64, _I64, _P, _I64, _P,   # q + strides, pool, rows, rope
+                                     _P, _I64, _P,
+                                     _I, _I, _I, _I, _I, _I, _I, _I, _F, _F,
+                                     _P, _I64, _I64, _I64,
+                                     _P, _SZ, _P, _P]),
+    "nvfp4kv_mla_decode_rope_workspace_size": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_SZ)]),
     "nvfp4kv_mla_decode_static": (_I, [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P,
                                        _I, _I, _I, _I, _I, _I, _I, _I, _F, _F,
                                        _P, _I64, _I64, _I64,

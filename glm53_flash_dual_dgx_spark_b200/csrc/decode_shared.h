@@ -43,7 +43,21 @@ struct DecodeArgs {
     uint8_t* qimg;    // [batch][groups][kQImageBytes]
     float* lse;       // optional [batch][q_len][heads]: natural-log sum of exp(bmm1_scale q.k)
     int32_t* err;
+    // rope side-pool (all null without one): 64 bf16 per pool row; the prepared rope part of q
+    // ([batch][groups][64][64] fp32, scaled like the Q terms) and the rope scores
+    // ([batch][groups][64][tiles_total * 128] fp32) the attention kernel adds to its scores
+    const uint16_t* rope_pool;
+    float* rope_q;
+    float* rope_logits;
 };
+
+// Workspace bytes the rope side of a decode adds to DecodePlan::ws_bytes (placed after it).
+inline size_t rope_q_bytes(const DecodePlan& pl, int batch) {
+    return static_cast<size_t>(batch) * pl.groups * kDecRows * 64 * sizeof(float);
+}
+inline size_t rope_logit_bytes(const DecodePlan& pl, int batch) {
+    return static_cast<size_t>(batch) * pl.groups * kDecRows * pl.tiles_total * kDecTile * sizeof(float);
+}
 
 // Launch `kernel` as a programmatic dependent of the kernel before it on `st`: it may start
 // while that kernel still runs, and reads that kernel's output only after griddepcontrol.wait.

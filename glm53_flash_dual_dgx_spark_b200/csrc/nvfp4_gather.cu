@@ -58,9 +58,12 @@ __device__ __forceinline__ float div_full(float a, float b) {
 // runtime:87-122.  One warp: the 656-byte row at `dst` re-encodes pool row clamp(src, 0, R-1).
 // kTritonDiv = false divides exactly (IEEE: the reference run on the CPU); true divides as the
 // reference compiled by Triton for the GPU does (div.full.f32), byte for byte.
+// `rope` (may be null): a rope side-pool of 64 bf16 per row (128 B), whose row src fills the
+// 656-byte row's rope bytes [528, 656); null writes them as zeros, as the reference does.
 template <bool kTritonDiv>
 __device__ __forceinline__ void gather_row_ds656(const uint8_t* __restrict__ pool, int64_t R, int64_t src,
-                                                 const float* table, uint8_t* __restrict__ dst, int lane) {
+                                                 const float* table, uint8_t* __restrict__ dst, int lane,
+                                                 const uint32_t* __restrict__ rope = nullptr) {
     src = src < 0 ? 0 : (src > R - 1 ? R - 1 : src);          // :98
     const uint8_t* row = pool + src * kRowBytes;
     const uint2 codes = ldg_nc_v2(row + 8 * lane);
@@ -87,20 +90,20 @@ __device__ __forceinline__ void gather_row_ds656(const uint8_t* __restrict__ poo
     }
     *reinterpret_cast<uint4*>(dst + 16 * lane) = make_uint4(o[0], o[1], o[2], o[3]);  // :117-120
     if ((lane & 7) == 0) *reinterpret_cast<float*>(dst + 512 + 4 * (lane >> 3)) = gscale;  // :114
-    *reinterpret_cast<uint32_t*>(dst + 528 + 4 * lane) = 0u;                           // :121-122
+    *reinterpret_cast<uint32_t*>(dst + 528 + 4 * lane) = rope ? __ldg(rope + src * 32 + lane) : 0u;  // :121-122
 }
 
 // Row r of `out` re-encodes pool row clamp(idx[r], 0, R-1).
 template <bool kTritonDiv>
 __global__ void __launch_bounds__(256)
 gather_ds656_kernel(const uint8_t* __restrict__ pool, int64_t R, const int32_t* __restrict__ idx,
-                    int64_t S, uint8_t* __restrict__ out) {
+                    int64_t S, uint8_t* __restrict__ out, const uint32_t* __restrict__ rope) {
     __shared__ float table[16];
     fill_code_table(table);
     const int lane = threadIdx.x & 31;
     const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r >= S) return;
-    gather_row_ds656<kTritonDiv>(pool, R, idx[r], table, out + r * kDsBytes, lane);
+    gather_row_ds656<kTritonDiv>(pool, R, idx[r], table, out + r * kDsBytes, lane, rope);
 }
 
 // ------------------------------------------------------------------ sync-free dedup
@@ -313,23 +316,44 @@ extern "C" int nvfp4kv_set_gather_division(int mode) {
 
 extern "C" int nvfp4kv_get_gather_division(void) { return nvfp4kv::g_gather_division.load(); }
 
-extern "C" int nvfp4kv_gather_ds656(const uint8_t* pool, int64_t pool_rows, const int32_t* idx,
-                                    int64_t num_rows, uint8_t* out, nvfp4kv_stream_t stream) {
-    using namespace nvfp4kv;
-    if (num_rows < 0) return fail(NVFP4KV_EINVAL, "nvfp4kv_gather_ds656: num_rows < 0");
+namespace nvfp4kv {
+namespace {
+
+int gather_ds656_impl(const char* name, const uint8_t* pool, const void* rope, int64_t pool_rows,
+                      const int32_t* idx, int64_t num_rows, uint8_t* out, nvfp4kv_stream_t stream) {
+    if (num_rows < 0) return fail(NVFP4KV_EINVAL, "%s: num_rows < 0", name);
     if (num_rows == 0) return NVFP4KV_OK;
-    if (!pool || !idx || !out) return fail(NVFP4KV_EINVAL, "nvfp4kv_gather_ds656: null pointer");
-    if (pool_rows <= 0) return fail(NVFP4KV_EINVAL, "nvfp4kv_gather_ds656: empty pool");
-    if (reinterpret_cast<uintptr_t>(pool) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
-        return fail(NVFP4KV_EINVAL, "nvfp4kv_gather_ds656: pool and out must be 16-byte aligned");
+    if (!pool || !idx || !out) return fail(NVFP4KV_EINVAL, "%s: null pointer", name);
+    if (pool_rows <= 0) return fail(NVFP4KV_EINVAL, "%s: empty pool", name);
+    if (reinterpret_cast<uintptr_t>(pool) % 16 || reinterpret_cast<uintptr_t>(out) % 16 ||
+        reinterpret_cast<uintptr_t>(rope) % 16)
+        return fail(NVFP4KV_EINVAL, "%s: pool, rope pool and out must be 16-byte aligned", name);
     const int warps = 8;
     const dim3 grid(static_cast<unsigned>((num_rows + warps - 1) / warps));
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const uint32_t* r = static_cast<const uint32_t*>(rope);
     if (g_gather_division.load() == NVFP4KV_DIV_TRITON)
-        gather_ds656_kernel<true><<<grid, warps * 32, 0, st>>>(pool, pool_rows, idx, num_rows, out);
+        gather_ds656_kernel<true><<<grid, warps * 32, 0, st>>>(pool, pool_rows, idx, num_rows, out, r);
     else
-        gather_ds656_kernel<false><<<grid, warps * 32, 0, st>>>(pool, pool_rows, idx, num_rows, out);
-    return check_launch("nvfp4kv_gather_ds656");
+        gather_ds656_kernel<false><<<grid, warps * 32, 0, st>>>(pool, pool_rows, idx, num_rows, out, r);
+    return check_launch(name);
+}
+
+}  // namespace
+}  // namespace nvfp4kv
+
+extern "C" int nvfp4kv_gather_ds656(const uint8_t* pool, int64_t pool_rows, const int32_t* idx,
+                                    int64_t num_rows, uint8_t* out, nvfp4kv_stream_t stream) {
+    return nvfp4kv::gather_ds656_impl("nvfp4kv_gather_ds656", pool, nullptr, pool_rows, idx, num_rows, out, stream);
+}
+
+extern "C" int nvfp4kv_gather_ds656_rope(const uint8_t* pool, const void* rope_pool, int64_t pool_rows,
+                                         const int32_t* idx, int64_t num_rows, uint8_t* out,
+                                         nvfp4kv_stream_t stream) {
+    if (!rope_pool && num_rows > 0)
+        return nvfp4kv::fail(NVFP4KV_EINVAL, "nvfp4kv_gather_ds656_rope: null rope pool");
+    return nvfp4kv::gather_ds656_impl("nvfp4kv_gather_ds656_rope", pool, rope_pool, pool_rows, idx, num_rows, out,
+                                      stream);
 }
 
 extern "C" int nvfp4kv_dequant_bf16(const uint8_t* pool, int64_t pool_rows, const void* rows,

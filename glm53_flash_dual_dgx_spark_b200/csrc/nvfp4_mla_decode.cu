@@ -219,18 +219,20 @@ int decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q
                 int kv_lora_rank, int sparse_topk, int page_size, int max_seq_len, float bmm1_scale,
                 float bmm2_scale, void* out, int64_t out_stride_b, int64_t out_stride_q,
                 int64_t out_stride_h, float* lse, void* workspace, size_t workspace_bytes,
-                int32_t* err_flag, nvfp4kv_stream_t stream) {
+                int32_t* err_flag, nvfp4kv_stream_t stream, const void* rope_pool = nullptr) {
     if (batch < 0) return fail(NVFP4KV_EINVAL, "mla_decode: batch < 0");
     if (batch == 0) return NVFP4KV_OK;
+    if (rope_pool && (head_dim_qk < NVFP4KV_LATENT + NVFP4KV_ROPE || reinterpret_cast<uintptr_t>(rope_pool) % 16))
+        return fail(NVFP4KV_EINVAL, "mla_decode_rope: head_dim_qk must be >= 576 and the rope pool 16-byte aligned");
     int page_shift = 0;
     int rc = check_decode_args(q, q_stride_b, q_stride_q, q_stride_h, pool, pool_rows, tables, seq_lens, batch,
                                q_len, num_heads, head_dim_qk, kv_lora_rank, sparse_topk, page_size, max_seq_len,
                                out, out_stride_b, out_stride_q, out_stride_h, &page_shift);
     if (rc != NVFP4KV_OK) return rc;
     const DecodePlan pl = make_decode_plan(batch, q_len, num_heads, max_seq_len, sparse_topk);
-    if (!workspace || workspace_bytes < pl.ws_bytes)
-        return fail(NVFP4KV_EWORKSPACE, "mla_decode: workspace %zu bytes < %zu required",
-                    workspace_bytes, pl.ws_bytes);
+    const size_t need = pl.ws_bytes + (rope_pool ? rope_q_bytes(pl, batch) + rope_logit_bytes(pl, batch) : 0);
+    if (!workspace || workspace_bytes < need)
+        return fail(NVFP4KV_EWORKSPACE, "mla_decode: workspace %zu bytes < %zu required", workspace_bytes, need);
     if (reinterpret_cast<uintptr_t>(workspace) % 256)
         return fail(NVFP4KV_EINVAL, "mla_decode: workspace must be 256-byte aligned");
     const size_t part_o_bytes = static_cast<size_t>(pl.splits) * batch * pl.groups * kNQ * kLatent * sizeof(float);
@@ -250,6 +252,12 @@ int decode_impl(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q
         a.out = out; a.o_sb = out_stride_b; a.o_sq = out_stride_q; a.o_sh = out_stride_h;
         a.part_o = part_o; a.part_ml = part_ml; a.err = err_flag; a.lse = lse;
         a.qimg = static_cast<uint8_t*>(workspace) + pl.part_bytes;
+        if (rope_pool) {
+            a.rope_pool = static_cast<const uint16_t*>(rope_pool);
+            a.rope_q = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.ws_bytes);
+            a.rope_logits = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.ws_bytes +
+                                                     rope_q_bytes(pl, batch));
+        }
         if ((rc = launch_decode_fp4(a, pl, st)) != NVFP4KV_OK) return rc;
     }
     if (pl.splits > 1) {
@@ -282,6 +290,39 @@ extern "C" int nvfp4kv_mla_decode(const void* q, int64_t q_stride_b, int64_t q_s
                                 page_size, max_seq_len, bmm1_scale, bmm2_scale, out, out_stride_b,
                                 out_stride_q, out_stride_h, nullptr, workspace, workspace_bytes, err_flag,
                                 stream);
+}
+
+extern "C" int nvfp4kv_mla_decode_rope(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,
+                                       const uint8_t* pool, int64_t pool_rows, const void* rope_pool,
+                                       const int32_t* tables, int64_t tables_stride,
+                                       const int32_t* seq_lens,
+                                       int batch, int q_len, int num_heads, int head_dim_qk, int kv_lora_rank,
+                                       int sparse_topk, int page_size, int max_seq_len,
+                                       float bmm1_scale, float bmm2_scale,
+                                       void* out, int64_t out_stride_b, int64_t out_stride_q, int64_t out_stride_h,
+                                       void* workspace, size_t workspace_bytes,
+                                       int32_t* err_flag, nvfp4kv_stream_t stream) {
+    if (!rope_pool && batch > 0) return nvfp4kv::fail(NVFP4KV_EINVAL, "mla_decode_rope: null rope pool");
+    return nvfp4kv::decode_impl(q, q_stride_b, q_stride_q, q_stride_h, pool, pool_rows, tables, tables_stride,
+                                seq_lens, batch, q_len, num_heads, head_dim_qk, kv_lora_rank, sparse_topk,
+                                page_size, max_seq_len, bmm1_scale, bmm2_scale, out, out_stride_b,
+                                out_stride_q, out_stride_h, nullptr, workspace, workspace_bytes, err_flag,
+                                stream, rope_pool);
+}
+
+extern "C" int nvfp4kv_mla_decode_rope_workspace_size(int batch, int q_len, int num_heads, int max_seq_len,
+                                                      int sparse_topk, size_t* bytes) {
+    using namespace nvfp4kv;
+    if (!bytes) return fail(NVFP4KV_EINVAL, "rope_workspace_size: null output");
+    if (batch < 0 || q_len < 1 || num_heads < 1 || max_seq_len < 0 || sparse_topk < 0)
+        return fail(NVFP4KV_EINVAL, "rope_workspace_size: bad shape");
+    if (batch == 0) {
+        *bytes = 0;
+        return NVFP4KV_OK;
+    }
+    const DecodePlan pl = make_decode_plan(batch, q_len, num_heads, max_seq_len, sparse_topk);
+    *bytes = pl.ws_bytes + rope_q_bytes(pl, batch) + rope_logit_bytes(pl, batch);
+    return NVFP4KV_OK;
 }
 
 extern "C" int nvfp4kv_mla_decode_lse(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,

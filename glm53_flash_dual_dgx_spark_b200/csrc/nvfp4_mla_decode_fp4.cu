@@ -137,6 +137,8 @@ struct Fp4Params {
     const uint8_t* qimg;
     float* lse;                    // optional [batch][q_len][heads] (single-split plans)
     int32_t* err;
+    const float* rope_logits;      // rope scores [units][64][rope_ld] (rope side-pool only)
+    int64_t rope_ld;
 };
 
 struct QPrepParams {
@@ -145,6 +147,7 @@ struct QPrepParams {
     int q_len, num_heads, groups;
     float scale_log2;
     uint8_t* qimg;
+    float* rope_q;   // [units][64][64] fp32: q's rope part times the row's 2^-e_n (null: no rope)
 };
 
 // Q of one query group (64 rows) -> four NVFP4 terms, written as the fused kernel's shared
@@ -155,7 +158,7 @@ struct QPrepParams {
 // ones.  One warp per row, one lane per 16-dim block: q_prep_row quantises row n of the
 // group from its 16 bf16 values per lane (u0, u1; zeros for rows past the group).
 __device__ __forceinline__ void q_prep_row(const QPrepParams& p, int unit, int n, bool real, int lane,
-                                           uint4 u0, uint4 u1) {
+                                           uint4 u0, uint4 u1, uint32_t rope_w) {
     const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
     float x[16];
     float amax = 0.0f;
@@ -172,6 +175,9 @@ __device__ __forceinline__ void q_prep_row(const QPrepParams& p, int unit, int n
     const float mul = ldexpf(1.0f, -e);
 #pragma unroll
     for (int j = 0; j < 16; ++j) x[j] *= mul;
+    if (p.rope_q)   // rope dims 512 + 2 lane, +1, on the same power-of-two scale as the terms
+        reinterpret_cast<float2*>(p.rope_q + (static_cast<size_t>(unit) * kNQ + n) * 64)[lane] =
+            make_float2(__uint_as_float(rope_w << 16) * mul, __uint_as_float(rope_w & 0xFFFF0000u) * mul);
     uint8_t* img = p.qimg + static_cast<size_t>(unit) * kQImageBytes;
     const int chunk = (lane & 15) >> 1;
 #pragma unroll
@@ -212,13 +218,82 @@ __global__ void __launch_bounds__(256) q_prep_kernel(const QPrepParams p) {
     const int rows_here = min(kNQ, p.q_len * p.num_heads - g * kNQ);
     const bool real = n < rows_here;
     uint4 u0 = make_uint4(0, 0, 0, 0), u1 = make_uint4(0, 0, 0, 0);
+    uint32_t rope_w = 0;
     if (real) {
         const int r = g * kNQ + n, qi = r / p.num_heads, h = r % p.num_heads;
-        const __nv_bfloat16* src = p.q + b * p.q_sb + qi * p.q_sq + h * p.q_sh + 16 * lane;
-        u0 = ldg_nc_v4(src);
-        u1 = ldg_nc_v4(src + 8);
+        const __nv_bfloat16* row = p.q + b * p.q_sb + qi * p.q_sq + h * p.q_sh;
+        u0 = ldg_nc_v4(row + 16 * lane);
+        u1 = ldg_nc_v4(row + 16 * lane + 8);
+        if (p.rope_q) rope_w = __ldg(reinterpret_cast<const uint32_t*>(row + kLatent) + lane);
     }
-    q_prep_row(p, unit, n, real, lane, u0, u1);
+    q_prep_row(p, unit, n, real, lane, u0, u1, rope_w);
+}
+
+// Rope scores of the rope side-pool: for query group `unit` (64 rows) and token position pos
+// of its entry, logits[unit][n][pos] = (q_rope[n] 2^-e_n) . k_rope[row(pos)] in fp32, in the
+// units of the attention kernel's raw scores (the Q terms carry the same 2^-e_n), 0 where the
+// position is masked.  One block per (unit, 128-token tile); thread = token x 32 rows.
+struct RopeParams {
+    const uint16_t* rope_pool;
+    int64_t pool_rows, num_pages;
+    const int32_t* tables;
+    int64_t tables_stride;
+    const int32_t* seq_lens;
+    int groups, page_shift, max_seq_len, tiles_total;
+    const float* rope_q;
+    float* logits;
+    int64_t ld;                        // tiles_total * 128
+};
+
+template <bool kSparse>
+__global__ void __launch_bounds__(256) rope_logits_kernel(const RopeParams p) {
+    __shared__ float4 qs[kNQ * 16];    // [64 rows][64 dims]
+    const int unit = blockIdx.x / p.tiles_total, tile = blockIdx.x % p.tiles_total;
+    const int b = unit / p.groups;
+    const float4* qsrc = reinterpret_cast<const float4*>(p.rope_q + static_cast<size_t>(unit) * kNQ * 64);
+    for (int k = threadIdx.x; k < kNQ * 16; k += blockDim.x) qs[k] = qsrc[k];
+    const int t = threadIdx.x & (kTile - 1), half = threadIdx.x >> 7;
+    const int pos = tile * kTile + t;
+    int L = __ldg(p.seq_lens + b);
+    L = L < 0 ? 0 : (L > p.max_seq_len ? p.max_seq_len : L);
+    int64_t row = -1;
+    if (pos < L) {
+        if constexpr (kSparse) {
+            const int idx = __ldg(p.tables + b * p.tables_stride + pos);
+            if (idx >= 0 && idx < p.pool_rows) row = idx;
+        } else {
+            const int pg = __ldg(p.tables + b * p.tables_stride + (pos >> p.page_shift));
+            if (pg >= 0 && pg < p.num_pages)
+                row = (static_cast<int64_t>(pg) << p.page_shift) | (pos & ((1 << p.page_shift) - 1));
+        }
+    }
+    float k[64];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const uint4 w = row >= 0 ? ldg_nc_v4(p.rope_pool + row * 64 + 8 * c) : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            k[8 * c + 2 * h] = __uint_as_float(ws[h] << 16);
+            k[8 * c + 2 * h + 1] = __uint_as_float(ws[h] & 0xFFFF0000u);
+        }
+    }
+    __syncthreads();
+    float* out = p.logits + (static_cast<int64_t>(unit) * kNQ + 32 * half) * p.ld + pos;
+#pragma unroll 2
+    for (int j = 0; j < 32; ++j) {
+        const float4* qr = qs + (32 * half + j) * 16;
+        float acc = 0.0f;
+#pragma unroll
+        for (int d4 = 0; d4 < 16; ++d4) {
+            const float4 qv = qr[d4];
+            acc = fmaf(qv.x, k[4 * d4], acc);
+            acc = fmaf(qv.y, k[4 * d4 + 1], acc);
+            acc = fmaf(qv.z, k[4 * d4 + 2], acc);
+            acc = fmaf(qv.w, k[4 * d4 + 3], acc);
+        }
+        out[static_cast<int64_t>(j) * p.ld] = acc;
+    }
 }
 
 __device__ __forceinline__ int page_id(const Fp4Params& p, const int* sidx, bool staged, int idx_base,
@@ -452,7 +527,7 @@ __device__ __forceinline__ void probs32(const float (&sraw)[32], const float* qs
 
 // kSparse: the table holds pool rows (top-k, -1 padded) instead of page ids; the tensor maps
 // have one-row boxes for the row gathers.
-template <bool kSparse, int kRing, int kVBuf>
+template <bool kSparse, int kRing, int kVBuf, bool kRope>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ CUtensorMap tm_codes,
                   const __grid_constant__ CUtensorMap tm_scales) {
@@ -840,6 +915,12 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
                 tmem_wait_ld();
 #pragma unroll
                 for (int j = 0; j < 32; ++j) sv[j] = __uint_as_float(a[j]) + __uint_as_float(c2[j]);
+                if constexpr (kRope) {   // + the rope scores of this token for the 32 rows
+                    const float* rl = p.rope_logits + (static_cast<int64_t>(bg) * kNQ + 32 * hh) * p.rope_ld +
+                                      start + i * kTile + t;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) sv[j] += __ldg(rl + j * p.rope_ld);
+                }
             };
             load_scores();
             const int pos = start + i * kTile + t;
@@ -1073,14 +1154,14 @@ int make_pool_map(CUtensorMap* m, const uint8_t* pool, int64_t pool_rows, uint32
     return NVFP4KV_OK;
 }
 
-template <bool kSparse, int kRing, int kVBuf>
+template <bool kSparse, int kRing, int kVBuf, bool kRope>
 int ensure_fp4_smem_attr() {
     static int done[64] = {0};
     constexpr int bytes = DecCfg<kRing, kVBuf>::kSmemBytes;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaGetDevice failed");
     if (dev >= 0 && dev < 64 && done[dev]) return NVFP4KV_OK;
-    const cudaError_t e = cudaFuncSetAttribute(decode_fp4_kernel<kSparse, kRing, kVBuf>,
+    const cudaError_t e = cudaFuncSetAttribute(decode_fp4_kernel<kSparse, kRing, kVBuf, kRope>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess)
         return fail(NVFP4KV_ECUDA, "cudaFuncSetAttribute(max dynamic smem %d): %s", bytes, cudaGetErrorString(e));
@@ -1090,12 +1171,12 @@ int ensure_fp4_smem_attr() {
 
 // The attention launch for one kernel shape (a programmatic dependent of the Q preparation:
 // its set-up overlaps that kernel's tail).
-template <bool kSparse, int kRing, int kVBuf>
+template <bool kSparse, int kRing, int kVBuf, bool kRope>
 int launch_attention(const Fp4Params& p, const CUtensorMap& tm_codes, const CUtensorMap& tm_scales, dim3 grid,
                      cudaStream_t st) {
     int rc;
-    if ((rc = ensure_fp4_smem_attr<kSparse, kRing, kVBuf>()) != NVFP4KV_OK) return rc;
-    const cudaError_t le = launch_dependent(decode_fp4_kernel<kSparse, kRing, kVBuf>, grid, dim3(kThreads),
+    if ((rc = ensure_fp4_smem_attr<kSparse, kRing, kVBuf, kRope>()) != NVFP4KV_OK) return rc;
+    const cudaError_t le = launch_dependent(decode_fp4_kernel<kSparse, kRing, kVBuf, kRope>, grid, dim3(kThreads),
                                             DecCfg<kRing, kVBuf>::kSmemBytes, st, p, tm_codes, tm_scales);
     if (le != cudaSuccess)
         return fail(NVFP4KV_ECUDA, "nvfp4kv_mla_decode: attention launch failed: %s", cudaGetErrorString(le));
@@ -1133,8 +1214,25 @@ int launch_decode_fp4(const DecodeArgs& a, const DecodePlan& pl, cudaStream_t st
     qp.q_len = a.q_len; qp.num_heads = a.num_heads; qp.groups = pl.groups;
     qp.scale_log2 = a.bmm1_scale * 1.4426950408889634f;
     qp.qimg = a.qimg;
+    qp.rope_q = a.rope_q;
     q_prep_kernel<<<a.batch * pl.groups * 8, 256, 0, st>>>(qp);
     if ((rc = check_launch("nvfp4kv_mla_decode (Q preparation)")) != NVFP4KV_OK) return rc;
+    if (a.rope_pool) {   // rope scores, after the Q preparation and before the attention
+        RopeParams rp{};
+        rp.rope_pool = a.rope_pool;
+        rp.pool_rows = a.pool_rows;
+        rp.num_pages = sparse ? 0 : a.pool_rows / a.page_size;
+        rp.tables = a.tables; rp.tables_stride = a.tables_stride; rp.seq_lens = a.seq_lens;
+        rp.groups = pl.groups; rp.page_shift = sparse ? 0 : a.page_shift;
+        rp.max_seq_len = sparse ? a.sparse_topk : a.max_seq_len;
+        rp.tiles_total = pl.tiles_total;
+        rp.rope_q = a.rope_q; rp.logits = a.rope_logits;
+        rp.ld = static_cast<int64_t>(pl.tiles_total) * kTile;
+        const dim3 rg(static_cast<unsigned>(static_cast<int64_t>(a.batch) * pl.groups * pl.tiles_total));
+        if (sparse) rope_logits_kernel<true><<<rg, 256, 0, st>>>(rp);
+        else rope_logits_kernel<false><<<rg, 256, 0, st>>>(rp);
+        if ((rc = check_launch("nvfp4kv_mla_decode_rope (rope scores)")) != NVFP4KV_OK) return rc;
+    }
     Fp4Params p{};
     p.pool = a.pool; p.pool_rows = a.pool_rows;
     p.tables = a.tables; p.tables_stride = a.tables_stride;
@@ -1152,15 +1250,24 @@ int launch_decode_fp4(const DecodeArgs& a, const DecodePlan& pl, cudaStream_t st
     p.qimg = a.qimg;
     p.lse = a.lse;
     p.err = a.err;
+    p.rope_logits = a.rope_logits;
+    p.rope_ld = static_cast<int64_t>(pl.tiles_total) * kTile;
     const dim3 grid(static_cast<unsigned>(a.batch * pl.groups * pl.splits));
     cudaEvent_t ev0, ev1;
     take_kernel_events(&ev0, &ev1);
     if (ev0 && cudaEventRecord(ev0, st) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaEventRecord failed");
     const bool shrt = short_ring(pl);
-    rc = sparse ? (shrt ? launch_attention<true, 2, 4>(p, tm_codes, tm_scales, grid, st)
-                        : launch_attention<true, 3, 2>(p, tm_codes, tm_scales, grid, st))
-                : (shrt ? launch_attention<false, 2, 4>(p, tm_codes, tm_scales, grid, st)
-                        : launch_attention<false, 3, 2>(p, tm_codes, tm_scales, grid, st));
+    if (a.rope_pool) {
+        rc = sparse ? (shrt ? launch_attention<true, 2, 4, true>(p, tm_codes, tm_scales, grid, st)
+                            : launch_attention<true, 3, 2, true>(p, tm_codes, tm_scales, grid, st))
+                    : (shrt ? launch_attention<false, 2, 4, true>(p, tm_codes, tm_scales, grid, st)
+                            : launch_attention<false, 3, 2, true>(p, tm_codes, tm_scales, grid, st));
+    } else {
+        rc = sparse ? (shrt ? launch_attention<true, 2, 4, false>(p, tm_codes, tm_scales, grid, st)
+                            : launch_attention<true, 3, 2, false>(p, tm_codes, tm_scales, grid, st))
+                    : (shrt ? launch_attention<false, 2, 4, false>(p, tm_codes, tm_scales, grid, st)
+                            : launch_attention<false, 3, 2, false>(p, tm_codes, tm_scales, grid, st));
+    }
     if (rc != NVFP4KV_OK) return rc;
     if (ev1 && cudaEventRecord(ev1, st) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaEventRecord failed");
     return NVFP4KV_OK;

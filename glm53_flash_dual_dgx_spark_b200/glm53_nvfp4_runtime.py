@@ -32,6 +32,7 @@ from . import _lib
 NV_BYTES = 288
 DS_BYTES = 656
 LATENT = 512
+ROPE = 64
 
 _ON = os.environ.get("GLM53_NVFP4_KV", "0") == "1"          # read once at import (runtime:29)
 
@@ -154,6 +155,33 @@ def write_nvfp4(kv_c: torch.Tensor, kv_cache: torch.Tensor, slot_mapping: torch.
     _lib.check(rc, "nvfp4kv_append")
 
 
+def write_nvfp4_rope(k_pe: torch.Tensor, rope_cache: torch.Tensor, slot_mapping: torch.Tensor) -> None:
+    """k_pe [T, 64] bf16 -> the rope side-pool rope_cache (any shape, 64 bf16 per token slot) at
+    slot_mapping; slots < 0 are skipped.  Not in the reference, which drops k_pe for its NoPE
+    model (patch_nvfp4_kv.py:70); for MLA models that keep a rope part, beside write_nvfp4."""
+    T = k_pe.shape[0]
+    if T == 0:
+        return
+    _require_cuda(k_pe, "k_pe")
+    _require_cuda(rope_cache, "rope_cache")
+    if k_pe.dtype != torch.bfloat16 or k_pe.dim() != 2 or k_pe.shape[1] < ROPE or k_pe.stride(1) != 1:
+        raise ValueError("k_pe must be bf16 [T, >=64] with a contiguous last dimension")
+    rope = rope_cache.view(-1, ROPE)
+    if rope.dtype != torch.bfloat16:
+        raise TypeError("rope_cache must be bf16")
+    slot = slot_mapping.reshape(-1).contiguous()
+    if slot.numel() != T:
+        raise ValueError(f"slot_mapping has {slot.numel()} entries for {T} tokens")
+    sdt = _lib.INDEX_I64 if slot.dtype == torch.int64 else _lib.INDEX_I32 if slot.dtype == torch.int32 else None
+    if sdt is None:
+        raise TypeError("slot_mapping must be int64 or int32")
+    dev = k_pe.device
+    with _on_device(dev):
+        rc = _lib.lib().nvfp4kv_append_rope(k_pe.data_ptr(), T, k_pe.stride(0), rope.data_ptr(), rope.shape[0],
+                                            slot.data_ptr(), sdt, _err_word(dev).data_ptr(), _stream(dev))
+    _lib.check(rc, "nvfp4kv_append_rope")
+
+
 # ------------------------------------------------------------------ 656-byte read path
 def set_gather_division(mode: str) -> None:
     """Division of the 656-byte row encoders, process-wide: "ieee" (exact; the reference's
@@ -174,8 +202,9 @@ if _GATHER_DIV != "ieee":
     set_gather_division(_GATHER_DIV)
 
 
-def _gather(pool: torch.Tensor, idx: torch.Tensor, out: torch.Tensor) -> None:
-    """NVFP4 pool rows at idx -> fp8_ds_mla 656-byte rows in out (runtime:128-131)."""
+def _gather(pool: torch.Tensor, idx: torch.Tensor, out: torch.Tensor, rope: torch.Tensor | None = None) -> None:
+    """NVFP4 pool rows at idx -> fp8_ds_mla 656-byte rows in out (runtime:128-131).  With a rope
+    side-pool ``rope`` (not in the reference) the rows' rope bytes carry its 64 bf16."""
     S = idx.shape[0]
     if S == 0:
         return
@@ -187,8 +216,15 @@ def _gather(pool: torch.Tensor, idx: torch.Tensor, out: torch.Tensor) -> None:
     idx = idx.contiguous()
     dev = pool.device
     with _on_device(dev):
-        rc = _lib.lib().nvfp4kv_gather_ds656(pool.data_ptr(), pool.shape[0], idx.data_ptr(), S,
-                                             out.data_ptr(), _stream(dev))
+        if rope is None:
+            rc = _lib.lib().nvfp4kv_gather_ds656(pool.data_ptr(), pool.shape[0], idx.data_ptr(), S,
+                                                 out.data_ptr(), _stream(dev))
+        else:
+            r = rope.reshape(-1, ROPE)
+            if r.dtype != torch.bfloat16 or r.shape[0] != pool.shape[0] or not r.is_contiguous():
+                raise ValueError("rope must be a contiguous bf16 [pool rows, 64] side-pool")
+            rc = _lib.lib().nvfp4kv_gather_ds656_rope(pool.data_ptr(), r.data_ptr(), pool.shape[0], idx.data_ptr(),
+                                                      S, out.data_ptr(), _stream(dev))
     _lib.check(rc, "nvfp4kv_gather_ds656")
 
 
@@ -370,7 +406,8 @@ def mla_decode(query: torch.Tensor, kv_cache: torch.Tensor, workspace_buffer: to
                qk_nope_head_dim: int, kv_lora_rank: int, qk_rope_head_dim: int,
                block_tables: torch.Tensor, seq_lens: torch.Tensor, max_seq_len: int,
                sparse_mla_top_k: int = 0, out: torch.Tensor | None = None,
-               bmm1_scale: float = 1.0, bmm2_scale: float = 1.0) -> torch.Tensor:
+               bmm1_scale: float = 1.0, bmm2_scale: float = 1.0,
+               rope_cache: torch.Tensor | None = None) -> torch.Tensor:
     """Fused NVFP4 gather + MLA decode (see module docstring).
 
     query: [B, q_len, H, kv_lora_rank + qk_rope_head_dim] bf16.
@@ -381,10 +418,12 @@ def mla_decode(query: torch.Tensor, kv_cache: torch.Tensor, workspace_buffer: to
       seq_lens = number of leading entries to use.
     Returns out [B, q_len, H, kv_lora_rank] bf16.  ``workspace_buffer`` is used for the
     split partials when it is large enough, else a persistent per-device buffer is.
+    rope_cache (not in the reference, whose model is NoPE): the rope side-pool, [num_pages,
+    page_size, 64] bf16 written by write_nvfp4_rope; the query's last 64 dims then meet it.
     """
     del qk_nope_head_dim  # accepted for signature compatibility; the absorbed MLA form ignores it
     return _decode(query, kv_cache, workspace_buffer, kv_lora_rank, qk_rope_head_dim, block_tables,
-                   seq_lens, max_seq_len, sparse_mla_top_k, out, bmm1_scale, bmm2_scale, None)
+                   seq_lens, max_seq_len, sparse_mla_top_k, out, bmm1_scale, bmm2_scale, None, rope_cache)
 
 
 def mla_decode_lse(query: torch.Tensor, kv_cache: torch.Tensor, workspace_buffer: torch.Tensor | None,
@@ -405,7 +444,7 @@ def mla_decode_lse(query: torch.Tensor, kv_cache: torch.Tensor, workspace_buffer
 
 
 def _decode(query, kv_cache, workspace_buffer, kv_lora_rank, qk_rope_head_dim, block_tables,
-            seq_lens, max_seq_len, sparse_mla_top_k, out, bmm1_scale, bmm2_scale, lse):
+            seq_lens, max_seq_len, sparse_mla_top_k, out, bmm1_scale, bmm2_scale, lse, rope_cache=None):
     _require_cuda(query, "query")
     _require_cuda(kv_cache, "kv_cache")
     if isinstance(bmm1_scale, torch.Tensor) or isinstance(bmm2_scale, torch.Tensor):
@@ -434,12 +473,27 @@ def _decode(query, kv_cache, workspace_buffer, kv_lora_rank, qk_rope_head_dim, b
         out = torch.empty(B, QL, H, LATENT, dtype=torch.bfloat16, device=query.device)
     elif out.shape != (B, QL, H, LATENT) or out.dtype != torch.bfloat16 or out.stride(3) != 1:
         raise ValueError("out must be bf16 [B, q_len, H, 512] with a contiguous last dimension")
+    rope = None
+    if rope_cache is not None:
+        if lse is not None:
+            raise ValueError("mla_decode_lse has no rope variant")
+        _require_cuda(rope_cache, "rope_cache")
+        rope = rope_cache.reshape(-1, ROPE)
+        if rope.dtype != torch.bfloat16 or rope.shape[0] != pool.shape[0] or not rope.is_contiguous():
+            raise ValueError("rope_cache must be a contiguous bf16 [pool rows, 64] side-pool")
     dev = query.device
     with _on_device(dev):
-        size_key = (B, QL, H, int(max_seq_len), int(sparse_mla_top_k), dev.index)
+        size_key = (B, QL, H, int(max_seq_len), int(sparse_mla_top_k), dev.index, rope is not None)
         ws_need = _ws_sizes.get(size_key)
         if ws_need is None:                      # the plan depends only on these and the device
-            ws_need = mla_decode_workspace_size(B, QL, H, max_seq_len, int(sparse_mla_top_k), dev)
+            if rope is None:
+                ws_need = mla_decode_workspace_size(B, QL, H, max_seq_len, int(sparse_mla_top_k), dev)
+            else:
+                n = ctypes.c_size_t(0)
+                _lib.check(_lib.lib().nvfp4kv_mla_decode_rope_workspace_size(
+                    B, QL, H, int(max_seq_len), int(sparse_mla_top_k), ctypes.byref(n)),
+                    "nvfp4kv_mla_decode_rope_workspace_size")
+                ws_need = int(n.value)
             _ws_sizes[size_key] = ws_need
         ws = _workspace(dev, ws_need, workspace_buffer)
         args = [query.data_ptr(), query.stride(0), query.stride(1), query.stride(2),
@@ -450,7 +504,9 @@ def _decode(query, kv_cache, workspace_buffer, kv_lora_rank, qk_rope_head_dim, b
                 float(bmm1_scale), float(bmm2_scale),
                 out.data_ptr(), out.stride(0), out.stride(1), out.stride(2)]
         tail = [ws.data_ptr() if ws is not None else None, ws_need, _err_word(dev).data_ptr(), _stream(dev)]
-        if lse is None:
+        if rope is not None:
+            rc = _lib.lib().nvfp4kv_mla_decode_rope(*args[:6], rope.data_ptr(), *args[6:], *tail)
+        elif lse is None:
             rc = _lib.lib().nvfp4kv_mla_decode(*args, *tail)
         else:
             rc = _lib.lib().nvfp4kv_mla_decode_lse(*args, lse.data_ptr(), *tail)

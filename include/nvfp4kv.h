@@ -217,6 +217,51 @@ int nvfp4kv_set_kernel_events(void* start, void* stop);
  * the kernel then returns normally, so the CUDA context stays usable. */
 int nvfp4kv_selftest_bounded_wait(int32_t* err_flag, nvfp4kv_stream_t stream);
 
+/*
+ * Rope side-pool.  No counterpart in the reference: its model is NoPE, its write seam drops
+ * k_pe (nvfp4-kv/patch_nvfp4_kv.py:70) and its 656-byte rows carry zero rope bytes
+ * (nvfp4-kv/glm53_nvfp4_runtime.py:121-122).  For MLA models whose keys carry a 64-d rope part
+ * the library keeps it beside the 288-byte pool in a pool of its own: [pool_rows, 64] bf16
+ * (128-byte rows, 16-byte aligned) addressed by the same token slots.  The 288-byte layout is
+ * unchanged, so every entry point above works on the same pool with or without it.
+ */
+
+/* k_pe [num_tokens, >= 64] bf16, row stride src_stride elements (inner dim contiguous) ->
+ * rope_pool[slot[t]].  slot < 0 skips the token; slot >= pool_rows skips it and sets
+ * NVFP4KV_DEVERR_BAD_SLOT (as nvfp4kv_append).  Call it beside nvfp4kv_append at the write seam. */
+int nvfp4kv_append_rope(const void* k_pe, int64_t num_tokens, int64_t src_stride, void* rope_pool,
+                        int64_t pool_rows, const void* slot_mapping, int slot_dtype,
+                        int32_t* err_flag, nvfp4kv_stream_t stream);
+
+/* nvfp4kv_gather_ds656 whose rows carry the rope part: bytes [528, 656) of row r are the 64
+ * bf16 of rope_pool[clamp(idx[r], 0, pool_rows - 1)] (the fp8_ds_mla format's rope field)
+ * instead of zeros; bytes [0, 528) as nvfp4kv_gather_ds656, division mode included. */
+int nvfp4kv_gather_ds656_rope(const uint8_t* pool, const void* rope_pool, int64_t pool_rows,
+                              const int32_t* idx, int64_t num_rows, uint8_t* out,
+                              nvfp4kv_stream_t stream);
+
+/* nvfp4kv_mla_decode with the rope part: q's dims [512, 576) (head_dim_qk >= 576) meet the
+ * rope rows, score = bmm1_scale * (q_nope . k + q_rope . k_rope); V is the latent as before.
+ * The rope scores are computed in fp32 by a kernel before the attention and added to its
+ * scores, so the workspace (nvfp4kv_mla_decode_rope_workspace_size) adds a 16 KB rope image
+ * per 64-row query group and 4 bytes per (query row, context position): 512 B per context
+ * token of a 64-head group (268 MB for batch 16 at 32K tokens).  Same errors as
+ * nvfp4kv_mla_decode, plus EINVAL for a null or unaligned rope pool. */
+int nvfp4kv_mla_decode_rope(const void* q, int64_t q_stride_b, int64_t q_stride_q, int64_t q_stride_h,
+                            const uint8_t* pool, int64_t pool_rows, const void* rope_pool,
+                            const int32_t* tables, int64_t tables_stride,
+                            const int32_t* seq_lens,
+                            int batch, int q_len, int num_heads, int head_dim_qk, int kv_lora_rank,
+                            int sparse_topk, int page_size, int max_seq_len,
+                            float bmm1_scale, float bmm2_scale,
+                            void* out, int64_t out_stride_b, int64_t out_stride_q, int64_t out_stride_h,
+                            void* workspace, size_t workspace_bytes,
+                            int32_t* err_flag, nvfp4kv_stream_t stream);
+
+/* Workspace bytes nvfp4kv_mla_decode_rope needs for this shape on the current device. */
+int nvfp4kv_mla_decode_rope_workspace_size(int batch, int q_len, int num_heads, int max_seq_len,
+                                           int sparse_topk, size_t* bytes);
+
 /* Capacity of the device scratch array behind nvfp4kv_mla_decode_static. */
 #define NVFP4KV_STATIC_SCRATCH_BYTES 33554432u
 

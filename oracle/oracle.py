@@ -143,13 +143,22 @@ def dequant(pool: np.ndarray, rows) -> np.ndarray:
     return out
 
 
-def gather_ds656(pool: np.ndarray, idx) -> np.ndarray:
-    """``_gather_kernel``: NVFP4 rows at ``idx`` -> [S, 656] fp8_ds_mla rows."""
+def gather_ds656(pool: np.ndarray, idx, rope=None) -> np.ndarray:
+    """``_gather_kernel``: NVFP4 rows at ``idx`` -> [S, 656] fp8_ds_mla rows.  ``rope`` (not in
+    the reference, which writes zeros there, runtime:121-122): a side-pool of 64 bf16 bit
+    patterns per row (uint16 [rows, 64]) whose clamped row fills the rope bytes [528, 656)."""
     flat = np.ascontiguousarray(pool.reshape(-1, NV_BYTES))
     idx = np.ascontiguousarray(np.asarray(idx).reshape(-1), dtype=np.int32)
     out = np.empty((idx.shape[0], DS_BYTES), dtype=np.uint8)
     _load().oracle_gather_ds656(_ptr(flat), flat.shape[0], _ptr(idx), idx.shape[0], _ptr(out))
+    if rope is not None:
+        src = np.clip(idx.astype(np.int64), 0, flat.shape[0] - 1)
+        out[:, 528:] = np.ascontiguousarray(np.asarray(rope, dtype=np.uint16)[src]).view(np.uint8)
     return out
+
+
+def bf16_bits_to_f32(bits) -> np.ndarray:
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
 
 
 def build_scratch(pool: np.ndarray, block_tables, sync_free_t: int = 192):
@@ -204,11 +213,13 @@ def token_rows(block_tables, seq_lens, page_size: int, sparse: bool, pool_rows: 
 
 def mla_decode(q, pool: np.ndarray, block_tables, seq_lens, *, sparse: bool,
                page_size: int = 64, bmm1_scale: float = 1.0, bmm2_scale: float = 1.0,
-               kv_lora_rank: int = LATENT, dtype=np.float64, return_lse: bool = False):
+               kv_lora_rank: int = LATENT, dtype=np.float64, return_lse: bool = False, rope=None):
     """Reference attention over the NVFP4 pool.
 
     q: [B, q_len, H, 576] (any float dtype; the last 64 rope dims multiply the all-zero
-    K rope of the 288-byte layout and so contribute nothing).  Query token i of a dense
+    K rope of the 288-byte layout and so contribute nothing, unless ``rope``, a side-pool of 64
+    bf16 bit patterns per row (uint16 [rows, 64]), gives the keys a rope part: then
+    score = q[:512] . k + q[512:576] . k_rope).  Query token i of a dense
     entry with q_len > 1 sees context tokens ``t < seq_len - (q_len - 1 - i)`` (causal MTP).
     Returns float [B, q_len, H, 512] (and the natural-log LSE [B, q_len, H] if asked).
     """
@@ -229,12 +240,16 @@ def mla_decode(q, pool: np.ndarray, block_tables, seq_lens, *, sparse: bool,
     for b in range(B):
         r, pos = rows[b]
         kv = dequant(flat_pool, r).astype(dtype)                 # [n, 512]
+        kr = bf16_bits_to_f32(np.asarray(rope)[r]).astype(dtype) if rope is not None else None
         for i in range(QL):
             lim = int(sl[b]) if sparse else int(sl[b]) - (QL - 1 - i)
             k = kv[pos < lim]
             if k.shape[0] == 0:
                 continue
-            s = (q[b, i, :, :kv_lora_rank].astype(dtype) @ k.T) * dtype(bmm1_scale)  # [H, vis]
+            s = q[b, i, :, :kv_lora_rank].astype(dtype) @ k.T               # [H, vis]
+            if kr is not None:
+                s = s + q[b, i, :, kv_lora_rank:kv_lora_rank + 64].astype(dtype) @ kr[pos < lim].T
+            s = s * dtype(bmm1_scale)
             m = s.max(axis=1, keepdims=True)
             p = np.exp(s - m)
             l = p.sum(axis=1, keepdims=True)

@@ -21,7 +21,7 @@ def declared_functions():
 def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     names = declared_functions()
-    assert len(names) == 16, names
+    assert len(names) == 20, names
     for n in names:
         assert hasattr(lib, n), n
     assert set(names) == set(_lib.SIGNATURES)
@@ -112,6 +112,30 @@ def test_static_decode_rejects_oversized_shapes_without_launch():
     assert call(454, q=None) == _lib.EINVAL           # a null pointer is reported, not the capacity
     assert call(454, pool=4100) == _lib.EINVAL        # so is a misaligned pool
     assert call(454, R=256) == _lib.EINVAL
+
+
+def test_rope_entry_points_check_arguments_without_launch():
+    lib = _lib.lib()
+    # append_rope: (k_pe, T, stride, rope_pool, rows, slots, slot dtype, err, stream)
+    assert lib.nvfp4kv_append_rope(None, 0, 64, None, 0, None, 0, None, None) == _lib.OK     # T == 0
+    assert lib.nvfp4kv_append_rope(4096, 4, 64, None, 16, 64, 0, None, None) == _lib.EINVAL  # null pool
+    assert lib.nvfp4kv_append_rope(4096, 4, 32, 4096, 16, 64, 0, None, None) == _lib.EINVAL  # stride < 64
+    assert lib.nvfp4kv_append_rope(4096, 4, 64, 4104, 16, 64, 0, None, None) == _lib.EINVAL  # unaligned pool
+    assert lib.nvfp4kv_gather_ds656_rope(4096, None, 16, 64, 4, 4096, None) == _lib.EINVAL     # null rope
+    assert lib.nvfp4kv_gather_ds656_rope(4096, 4104, 16, 64, 4, 4096, None) == _lib.EINVAL     # unaligned
+
+    def dec(rope=4096, D=576, ws=None, wsb=0):
+        return lib.nvfp4kv_mla_decode_rope(4096, 64 * 576, 64 * 576, 576, 4096, 1024, rope, 64, 16, 64,
+                                           2, 1, 64, D, 512, 0, 64, 1024, 1.0, 1.0,
+                                           4096, 64 * 512, 64 * 512, 512, ws, wsb, None, None)
+    assert dec(rope=None) == _lib.EINVAL
+    assert dec(D=512) == _lib.EINVAL                     # no rope dims in q
+    assert dec() == _lib.EWORKSPACE
+    plain, rope = ctypes.c_size_t(), ctypes.c_size_t()
+    assert lib.nvfp4kv_mla_decode_workspace_size(2, 1, 64, 1024, 0, ctypes.byref(plain)) == _lib.OK
+    assert lib.nvfp4kv_mla_decode_rope_workspace_size(2, 1, 64, 1024, 0, ctypes.byref(rope)) == _lib.OK
+    # + a 64 x 64 fp32 rope image per query group + 64 rows x 1024 positions of fp32 scores
+    assert rope.value == plain.value + 2 * 64 * 64 * 4 + 2 * 64 * 1024 * 4
 
 
 def test_dedup_workspace_and_argument_checks_without_launch():
