@@ -1222,6 +1222,28 @@ def gpu_reference_dedup(torch, pool, tabs_d, ours_us):
             "ours_step_us": round(ours_us, 2), "speedup": round(us / ours_us, 2)}
 
 
+def host_link_gbs(torch, dev, h2d_step: int, d2h_step: int) -> dict:
+    """The box's pinned host<->device copy rates: one 64 MiB copy each way, and one copy of a
+    step's input / output size, CUDA events on one stream (what bounds the e2e figure)."""
+    res = {}
+    for name, n in (("h2d_64MiB", 64 << 20), ("h2d_step", h2d_step), ("d2h_64MiB", 64 << 20), ("d2h_step", d2h_step)):
+        h = torch.empty(n, dtype=torch.uint8).pin_memory()
+        d = torch.empty(n, dtype=torch.uint8, device=dev)
+        src, dst = (h, d) if name.startswith("h2d") else (d, h)
+        for _ in range(3):
+            dst.copy_(src, non_blocking=True)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(10):
+            dst.copy_(src, non_blocking=True)
+        b.record()
+        b.synchronize()
+        us = a.elapsed_time(b) / 10 * 1e3
+        res[name] = {"bytes": n, "us": round(us, 2), "GBs": round(n / us / 1e3, 1)}
+    return res
+
+
 # ---------------------------------------------------------------------------- checks of the results
 def fp32_check(torch, rt, wl, ly, seqs, sm):
     """Layer `ly`'s decode output for sequences `seqs` against the exact dequantised attention in
@@ -1460,6 +1482,7 @@ def main() -> None:
         call(ly)
     e2e_serial = e2e_run(False)
     e2e_value = e2e_run(True)
+    link = host_link_gbs(torch, dev, h2d, d2h)
 
     # ---- the attention kernel alone: CUDA events recorded by the library immediately around
     # it (on its stream), over a separate run of the same steps
@@ -1507,7 +1530,7 @@ def main() -> None:
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                     "pipeline": "copies of step k+1 / k-1 overlap the decode of step k (3 streams)",
-                    "serial_value": round(e2e_serial, 2)},
+                    "serial_value": round(e2e_serial, 2), "host_link": link},
             "gpu_launches": args.steps * launches_per_step,
             "clocks": sampler.summary(t0, t1),
             "device_errors": errors,

@@ -60,6 +60,10 @@ SIGNATURES = {
                                      _P, _I64, _I64, _I64,
                                      _P, _SZ, _P, _P]),
     "nvfp4kv_mla_decode_rope_workspace_size": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_SZ)]),
+    "nvfp4kv_index_append": (_I, [_P, _I64, _I64, _P, _I64, _P, _I, _P, _P]),
+    "nvfp4kv_index_topk": (_I, [_P, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _P,
+                                _I, _I, _I, _I, _I, _P, _P, _P, _SZ, _P, _P]),
+    "nvfp4kv_index_topk_workspace_size": (_I, [_I, _I, ctypes.POINTER(_SZ)]),
     "nvfp4kv_mla_decode_static": (_I, [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P,
                                        _I, _I, _I, _I, _I, _I, _I, _I, _F, _F,
                                        _P, _I64, _I64, _I64,

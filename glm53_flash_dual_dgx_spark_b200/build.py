@@ -20,7 +20,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libnvfp4kv.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["abi_common.cu", "nvfp4_append.cu", "nvfp4_gather.cu", "nvfp4_rope.cu", "nvfp4_mla_decode.cu",
+SOURCES = ["abi_common.cu", "nvfp4_append.cu", "nvfp4_gather.cu", "nvfp4_rope.cu", "nvfp4_indexer.cu", "nvfp4_mla_decode.cu",
            "nvfp4_mla_decode_fp4.cu", "nvfp4_mla_decode_static.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",

@@ -201,8 +201,77 @@ void launch_append(const void* kv_c, int64_t T, int64_t stride, uint8_t* pool, i
         append_kernel<DT, SLOT_DT, false><<<grid, warps * 32, 0, st>>>(src, T, stride, pool, rows, slot, err);
 }
 
+// Indexer keys: a 128-d key per token quantised by the same rule as the latent rows (per-16
+// scale e4m3(max(amax / 6, 1e-8)), codes by the `<` ladder with ties up), into a 72-byte row:
+// bytes [0, 64) codes (byte i = code[2i] | code[2i+1] << 4), bytes [64, 72) the 8 block
+// scales.  A half-warp per token, a lane per 8 elements (a block spans two lanes); the exact
+// compare ladder throughout.  Lanes of a token past T compute on zeros and store nothing (the
+// block's partner shuffle needs every lane).
+template <int SLOT_DT, bool VEC>
+__global__ void __launch_bounds__(256)
+index_append_kernel(const uint16_t* __restrict__ k, int64_t T, int64_t stride, uint8_t* __restrict__ pool,
+                    int64_t rows, const void* __restrict__ slot_mapping, int32_t* __restrict__ err) {
+    const int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
+    const int l = threadIdx.x & 15;
+    const bool live = t < T;
+    int64_t slot = -1;
+    float x[8];
+    if (live) {
+        slot = SLOT_DT == NVFP4KV_INDEX_I64 ? static_cast<const int64_t*>(slot_mapping)[t]
+                                            : static_cast<const int32_t*>(slot_mapping)[t];
+        unpack8<NVFP4KV_DTYPE_BF16>(load8_raw<VEC>(k + t * stride + 8 * l), x);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[j] = 0.0f;
+    }
+    uint8_t sb;
+    const uint32_t codes = quant_half(x, sb);
+    if (!live || slot < 0) return;
+    if (slot >= rows) {
+        if (l == 0) set_error(err, NVFP4KV_DEVERR_BAD_SLOT);
+        return;
+    }
+    uint8_t* row = pool + slot * NVFP4KV_INDEX_ROW_BYTES;
+    *reinterpret_cast<uint32_t*>(row + 4 * l) = codes;
+    if ((l & 1) == 0) row[64 + (l >> 1)] = sb;
+}
+
+template <int SLOT_DT>
+void launch_index_append(const uint16_t* k, int64_t T, int64_t stride, uint8_t* pool, int64_t rows,
+                         const void* slot, int32_t* err, bool vec, cudaStream_t st) {
+    const dim3 grid(static_cast<unsigned>((T * 16 + 255) / 256));
+    if (vec) index_append_kernel<SLOT_DT, true><<<grid, 256, 0, st>>>(k, T, stride, pool, rows, slot, err);
+    else index_append_kernel<SLOT_DT, false><<<grid, 256, 0, st>>>(k, T, stride, pool, rows, slot, err);
+}
+
 }  // namespace
 }  // namespace nvfp4kv
+
+extern "C" int nvfp4kv_index_append(const void* k, int64_t num_tokens, int64_t src_stride, uint8_t* index_pool,
+                                    int64_t pool_rows, const void* slot_mapping, int slot_dtype,
+                                    int32_t* err_flag, nvfp4kv_stream_t stream) {
+    using namespace nvfp4kv;
+    if (num_tokens < 0) return fail(NVFP4KV_EINVAL, "nvfp4kv_index_append: num_tokens < 0");
+    if (num_tokens == 0) return NVFP4KV_OK;
+    if (!k || !index_pool || !slot_mapping) return fail(NVFP4KV_EINVAL, "nvfp4kv_index_append: null pointer");
+    if (src_stride < NVFP4KV_INDEX_DIM)
+        return fail(NVFP4KV_EINVAL, "nvfp4kv_index_append: src_stride %lld < 128", (long long)src_stride);
+    if (pool_rows <= 0) return fail(NVFP4KV_EINVAL, "nvfp4kv_index_append: empty index pool");
+    if (reinterpret_cast<uintptr_t>(index_pool) % 8 || reinterpret_cast<uintptr_t>(k) % 2)
+        return fail(NVFP4KV_EINVAL, "nvfp4kv_index_append: index pool must be 8-byte and k 2-byte aligned");
+    if (slot_dtype != NVFP4KV_INDEX_I64 && slot_dtype != NVFP4KV_INDEX_I32)
+        return fail(NVFP4KV_EINVAL, "nvfp4kv_index_append: slot dtype must be int64 or int32");
+    const bool vec = reinterpret_cast<uintptr_t>(k) % 16 == 0 && src_stride % 8 == 0;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const uint16_t* src = static_cast<const uint16_t*>(k);
+    if (slot_dtype == NVFP4KV_INDEX_I64)
+        launch_index_append<NVFP4KV_INDEX_I64>(src, num_tokens, src_stride, index_pool, pool_rows, slot_mapping,
+                                               err_flag, vec, st);
+    else
+        launch_index_append<NVFP4KV_INDEX_I32>(src, num_tokens, src_stride, index_pool, pool_rows, slot_mapping,
+                                               err_flag, vec, st);
+    return check_launch("nvfp4kv_index_append");
+}
 
 extern "C" int nvfp4kv_append(const void* kv_c, int kv_dtype, int64_t num_tokens, int64_t src_stride,
                               uint8_t* pool, int64_t pool_rows, const void* slot_mapping,

@@ -512,3 +512,86 @@ def _decode(query, kv_cache, workspace_buffer, kv_lora_rank, qk_rope_head_dim, b
             rc = _lib.lib().nvfp4kv_mla_decode_lse(*args, lse.data_ptr(), *tail)
     _lib.check(rc, "nvfp4kv_mla_decode")
     return out
+
+
+# ------------------------------------------------------------------ indexer K-pool
+INDEX_DIM = 128
+INDEX_ROW_BYTES = 72
+
+
+def index_append(k: torch.Tensor, index_cache: torch.Tensor, slot_mapping: torch.Tensor) -> None:
+    """Indexer keys k [T, 128] bf16 -> NVFP4 72-byte rows of index_cache (any shape, 72 bytes per
+    token slot) at slot_mapping; slots < 0 are skipped.  The reference keeps its indexer keys in
+    an fp8 pool (PLAN.md:29); this is the FP4 pool its README (:321) leaves to sm_100."""
+    T = k.shape[0]
+    if T == 0:
+        return
+    _require_cuda(k, "k")
+    _require_cuda(index_cache, "index_cache")
+    if k.dtype != torch.bfloat16 or k.dim() != 2 or k.shape[1] < INDEX_DIM or k.stride(1) != 1:
+        raise ValueError("k must be bf16 [T, >=128] with a contiguous last dimension")
+    pool = index_cache.view(-1, INDEX_ROW_BYTES)
+    if pool.dtype != torch.uint8:
+        raise TypeError("index_cache must be uint8")
+    slot = slot_mapping.reshape(-1).contiguous()
+    if slot.numel() != T:
+        raise ValueError(f"slot_mapping has {slot.numel()} entries for {T} tokens")
+    sdt = _lib.INDEX_I64 if slot.dtype == torch.int64 else _lib.INDEX_I32 if slot.dtype == torch.int32 else None
+    if sdt is None:
+        raise TypeError("slot_mapping must be int64 or int32")
+    dev = k.device
+    with _on_device(dev):
+        rc = _lib.lib().nvfp4kv_index_append(k.data_ptr(), T, k.stride(0), pool.data_ptr(), pool.shape[0],
+                                             slot.data_ptr(), sdt, _err_word(dev).data_ptr(), _stream(dev))
+    _lib.check(rc, "nvfp4kv_index_append")
+
+
+def index_topk(q: torch.Tensor, weights: torch.Tensor, index_cache: torch.Tensor, block_tables: torch.Tensor,
+               seq_lens: torch.Tensor, max_seq_len: int, topk: int = 2048,
+               out_rows: torch.Tensor | None = None, out_count: torch.Tensor | None = None):
+    """The DSA indexer's selection over the NVFP4 indexer pool: per entry b, the pool rows of the
+    topk positions s < seq_lens[b] with the highest sum_h weights[b, h] * max(q[b, h] . k[s], 0),
+    in ascending position order (-1 padded), and their count min(seq_lens[b], topk).
+    q [B, 64, 128] bf16, weights [B, 64] fp32, block_tables [B, pages] page ids.  The two
+    results are the sparse tables and seq_lens mla_decode(..., sparse_mla_top_k=topk) takes.
+    No host synchronisation; the score workspace is a persistent per-device buffer."""
+    _require_cuda(q, "q")
+    B = q.shape[0]
+    if q.dtype != torch.bfloat16 or q.dim() != 3 or q.shape[2] != INDEX_DIM or q.stride(2) != 1:
+        raise ValueError("q must be bf16 [B, 64, 128] with a contiguous last dimension")
+    if weights.dtype != torch.float32 or weights.shape[0] != B or weights.stride(1) != 1:
+        raise ValueError("weights must be float32 [B, 64]")
+    pool = index_cache.view(-1, INDEX_ROW_BYTES)
+    page_size = index_cache.shape[-2] if index_cache.dim() >= 3 else 64
+    if block_tables.dtype != torch.int32 or seq_lens.dtype != torch.int32:
+        raise TypeError("block_tables and seq_lens must be int32")
+    dev = q.device
+    if out_rows is None:
+        out_rows = torch.empty(B, topk, dtype=torch.int32, device=dev)
+    if out_count is None:
+        out_count = torch.empty(B, dtype=torch.int32, device=dev)
+    with _on_device(dev):
+        need = ctypes.c_size_t(0)
+        _lib.check(_lib.lib().nvfp4kv_index_topk_workspace_size(B, int(max_seq_len), ctypes.byref(need)),
+                   "nvfp4kv_index_topk_workspace_size")
+        key = ("index_ws", dev.index)
+        ws = _bufs.get(key)
+        if ws is None or ws.numel() < need.value:
+            ws = torch.empty(max(need.value, 1 << 16), dtype=torch.uint8, device=dev)
+            _bufs[key] = ws
+        rc = _lib.lib().nvfp4kv_index_topk(q.data_ptr(), q.stride(0), q.stride(1), weights.data_ptr(),
+                                           weights.stride(0), pool.data_ptr(), pool.shape[0],
+                                           block_tables.data_ptr(), block_tables.stride(0),
+                                           seq_lens.contiguous().data_ptr(), B, q.shape[1], int(page_size),
+                                           int(max_seq_len), int(topk), out_rows.data_ptr(), out_count.data_ptr(),
+                                           ws.data_ptr(), ws.numel(), _err_word(dev).data_ptr(), _stream(dev))
+    _lib.check(rc, "nvfp4kv_index_topk")
+    return out_rows, out_count
+
+
+def index_scores_buffer(device=None) -> torch.Tensor | None:
+    """The score workspace of the last index_topk on `device` (float32, [B, ceil(max_seq_len /
+    128) * 128] row-major), for inspection."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    ws = _bufs.get(("index_ws", dev.index))
+    return None if ws is None else ws.view(torch.float32)

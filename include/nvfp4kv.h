@@ -31,6 +31,8 @@ extern "C" {
 #define NVFP4KV_DS_BYTES 656
 #define NVFP4KV_LATENT 512
 #define NVFP4KV_ROPE 64
+#define NVFP4KV_INDEX_DIM 128       /* indexer key dims */
+#define NVFP4KV_INDEX_ROW_BYTES 72  /* NVFP4 indexer key row: 64 B codes + 8 e4m3 scales */
 
 /* host-side return codes */
 #define NVFP4KV_OK 0
@@ -261,6 +263,44 @@ int nvfp4kv_mla_decode_rope(const void* q, int64_t q_stride_b, int64_t q_stride_
 /* Workspace bytes nvfp4kv_mla_decode_rope needs for this shape on the current device. */
 int nvfp4kv_mla_decode_rope_workspace_size(int batch, int q_len, int num_heads, int max_seq_len,
                                            int sparse_topk, size_t* bytes);
+
+/*
+ * Indexer K-pool: the keys of the sparse-attention (DSA) lightning indexer whose top-k rows the
+ * sparse decode reads.  The reference keeps them an fp8 pool ("stays fp8", nvfp4-kv/PLAN.md:29;
+ * "FP4 indexer keys need sm_100", README.md:321) and takes its top-k from vLLM's indexer
+ * (topk_indices_buffer, vllm-0.22 flashinfer_mla_sparse.py:327-337).  Here the 128-d keys are
+ * NVFP4, 72-byte rows [num_pages, page_size, 72] (bytes [0, 64) codes, byte i = code[2i] |
+ * code[2i+1] << 4; bytes [64, 72) e4m3 scales, scale g for elements [16g, 16g + 16)),
+ * addressed by the same token slots as the 288-byte pool and quantised by the same rule.
+ */
+
+/* k [num_tokens, >= 128] bf16, row stride src_stride elements -> index_pool[slot[t]];
+ * slot < 0 skips, slot >= pool_rows skips and sets NVFP4KV_DEVERR_BAD_SLOT. */
+int nvfp4kv_index_append(const void* k, int64_t num_tokens, int64_t src_stride, uint8_t* index_pool,
+                         int64_t pool_rows, const void* slot_mapping, int slot_dtype,
+                         int32_t* err_flag, nvfp4kv_stream_t stream);
+
+/*
+ * Top-k selection by the DSA indexer rule (DeepSeek-V3.2's, as vLLM 0.22 states it):
+ *   score[b, s] = sum_h weights[b, h] * max(q[b, h, :] . k[s, :], 0)
+ * over the visible positions s < seq_lens[b] of entry b (a page-table entry, as in dense
+ * decode), k the exactly dequantised keys, fp32 accumulation.  out_rows[b, :] receives the pool
+ * rows of the topk highest-scoring positions in ascending position order (ties at the
+ * threshold go to the lower positions), -1 after out_count[b] = min(seq_lens[b], topk) and for
+ * a position on a missing page: exactly the sparse tables and seq_lens nvfp4kv_mla_decode takes.
+ * q: bf16 [batch, 64 heads, 128] with element strides (q_stride_b, q_stride_h), 16-byte
+ * aligned; weights fp32 [batch, 64], row stride weights_stride; workspace: the scores,
+ * nvfp4kv_index_topk_workspace_size() bytes, 16-byte aligned.
+ */
+int nvfp4kv_index_topk(const void* q, int64_t q_stride_b, int64_t q_stride_h, const float* weights,
+                       int64_t weights_stride, const uint8_t* index_pool, int64_t pool_rows,
+                       const int32_t* tables, int64_t tables_stride, const int32_t* seq_lens,
+                       int batch, int num_heads, int page_size, int max_seq_len, int topk,
+                       int32_t* out_rows, int32_t* out_count, void* workspace, size_t workspace_bytes,
+                       int32_t* err_flag, nvfp4kv_stream_t stream);
+
+/* Workspace bytes of nvfp4kv_index_topk: 4 per (entry, position up to max_seq_len rounded to 128). */
+int nvfp4kv_index_topk_workspace_size(int batch, int max_seq_len, size_t* bytes);
 
 /* Capacity of the device scratch array behind nvfp4kv_mla_decode_static. */
 #define NVFP4KV_STATIC_SCRATCH_BYTES 33554432u

@@ -258,3 +258,76 @@ def mla_decode(q, pool: np.ndarray, block_tables, seq_lens, *, sparse: bool,
     if return_lse:
         return out, lse
     return out
+
+
+# ---------------------------------------------------------------- indexer K-pool
+INDEX_DIM = 128
+INDEX_ROW = 72
+
+
+def index_quant(k) -> np.ndarray:
+    """128-d indexer keys [T, 128] -> 72-byte NVFP4 rows [T, 72] by the latent rows' rule
+    (``_quant_kernel``, runtime:37-65): blocks of 16 are independent, so a key is quantised as
+    the first 128 elements of a zero-padded 512-element row and its 64 code bytes and 8 scale
+    bytes are kept."""
+    try:
+        import torch
+
+        if isinstance(k, torch.Tensor):
+            k = k.detach().cpu()
+            pad = torch.zeros(k.shape[0], LATENT, dtype=k.dtype)
+            pad[:, :INDEX_DIM] = k[:, :INDEX_DIM]
+            rows = quant_new(pad)
+        else:
+            raise TypeError
+    except (ImportError, TypeError):  # pragma: no cover
+        raise TypeError("index_quant takes a bf16/fp16 torch tensor")
+    return np.concatenate([rows[:, :64], rows[:, 256:264]], axis=1)
+
+
+def index_dequant(rows72: np.ndarray) -> np.ndarray:
+    """72-byte indexer rows -> float32 [n, 128] (code x scale, exact)."""
+    r = np.asarray(rows72, dtype=np.uint8).reshape(-1, INDEX_ROW)
+    full = np.zeros((r.shape[0], NV_BYTES), dtype=np.uint8)
+    full[:, :64] = r[:, :64]
+    full[:, 256:264] = r[:, 64:72]
+    return dequant(full, np.arange(r.shape[0]))[:, :INDEX_DIM]
+
+
+def index_scores(q, weights, pool72: np.ndarray, tables, seq_lens, page_size: int = 64):
+    """Per entry b, float64 scores of its visible positions s < seq_lens[b]:
+    sum_h w[b, h] * max(q[b, h] . k[s], 0) (DeepSeek-V3.2's indexer rule), -inf where the
+    position's page is outside the pool."""
+    try:
+        import torch
+
+        if isinstance(q, torch.Tensor):
+            q = q.detach().float().cpu().numpy()
+        if isinstance(weights, torch.Tensor):
+            weights = weights.detach().float().cpu().numpy()
+    except ImportError:  # pragma: no cover
+        pass
+    flat = np.asarray(pool72, dtype=np.uint8).reshape(-1, INDEX_ROW)
+    keys = index_dequant(flat).astype(np.float64)
+    num_pages = flat.shape[0] // page_size
+    out = []
+    for b in range(len(seq_lens)):
+        n = int(seq_lens[b])
+        pos = np.arange(n)
+        pages = np.asarray(tables[b])[pos // page_size].astype(np.int64)
+        ok = (pages >= 0) & (pages < num_pages)
+        rows = np.where(ok, pages * page_size + pos % page_size, 0)
+        dots = keys[rows] @ np.asarray(q[b], dtype=np.float64).T          # [n, H]
+        s = np.maximum(dots, 0.0) @ np.asarray(weights[b], dtype=np.float64)
+        out.append(np.where(ok, s, -np.inf))
+    return out
+
+
+def index_select(scores_b: np.ndarray, topk: int) -> np.ndarray:
+    """Positions of the topk largest scores, ascending; ties at the threshold to the lowest
+    positions (the selection rule of nvfp4kv_index_topk)."""
+    n = scores_b.shape[0]
+    if n <= topk:
+        return np.arange(n)
+    order = np.lexsort((np.arange(n), -scores_b))        # score descending, then position
+    return np.sort(order[:topk])

@@ -21,7 +21,7 @@ def declared_functions():
 def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     names = declared_functions()
-    assert len(names) == 20, names
+    assert len(names) == 23, names
     for n in names:
         assert hasattr(lib, n), n
     assert set(names) == set(_lib.SIGNATURES)
