@@ -67,6 +67,12 @@ WORKLOADS = {
                        "entries from a 300,000-token context of a 2,713,846-token pool (10 % -1 padding), "
                        "deduplicated on the device and gathered into 656 B rows",
                   B=2048, H=0, QL=0, ctx=300000, topk=2048, pool_tokens=2713846, dedup=True),
+    # config 3's full sparse read path: the DSA indexer's top-2048 selection over NVFP4 indexer
+    # keys (the indexer K-pool), then the fused sparse decode on the rows it picked
+    "dsa": dict(desc="config 3 with its indexer: batch 16, 64 heads, 128K-token sequences on shuffled pages; "
+                     "top-2048 rows chosen by the DSA indexer rule over NVFP4 indexer keys (64 heads x 128), "
+                     "then the fused sparse decode",
+                B=16, H=64, QL=1, ctx=131072, topk=2048, dsa=True),
     # config 5's attention half, as the reference's large-step read path runs it: every new token
     # attends the top-2048 rows its indexer picks from its causal window (the prior 300,000
     # tokens of its sequence and the chunk up to itself); one step = one layer for all 32,768
@@ -218,7 +224,12 @@ DEDUP_ENTRY_BYTES = 4 + 4          # entry read, table written
 DEDUP_ROW_BYTES = NV_BYTES + 656    # distinct row read, 656 B row written
 
 
+INDEX_ROW_BYTES = 72
+
+
 def kv_bytes_per_step(wl) -> int:
+    if wl.get("dsa"):   # every visible indexer key once, then the selected latent rows
+        return wl["B"] * wl["ctx"] * INDEX_ROW_BYTES + wl["B"] * wl["topk"] * NV_BYTES
     if wl.get("prefill"):
         return wl["B"] * wl["ctx"] * wl["topk"] * NV_BYTES
     if wl.get("dedup"):
@@ -238,6 +249,71 @@ def kv_bytes_per_step(wl) -> int:
 LONG_PIECES_PER_RANK = 48
 
 
+def long_rank_pool(rt, torch, wl, dev, rank, world, seed):
+    """Rank ``rank``'s share of the config-4 job: (plan, its units, its pool [pages, 64, 288]
+    written by the append kernel, each unit's page list in token order).  Deterministic in
+    (seed, rank, world), so any rank can rebuild any other rank's pool."""
+    from glm53_flash_dual_dgx_spark_b200 import partition as P
+
+    plan = P.plan(wl["lens"], world * LONG_PIECES_PER_RANK, 64, q_len=wl["QL"])
+    units = [u for part in plan[rank * LONG_PIECES_PER_RANK:(rank + 1) * LONG_PIECES_PER_RANK] for u in part]
+    pages = [(u.tokens + 63) // 64 for u in units]
+    pool = torch.empty(sum(pages), 64, NV_BYTES, dtype=torch.uint8, device=dev)
+    gd = torch.Generator(device=dev).manual_seed(seed * 1000 + rank)
+    for c in range(0, pool.shape[0] * 64, 1 << 20):
+        n = min(1 << 20, pool.shape[0] * 64 - c)
+        x = torch.randn(n, 512, device=dev, generator=gd).to(torch.bfloat16)
+        rt.write_nvfp4(x, pool, torch.arange(c, c + n, device=dev))
+    g = torch.Generator().manual_seed(seed * 1000 + rank)
+    perm = torch.randperm(pool.shape[0], generator=g).to(torch.int32)
+    tables, k = [], 0
+    for m in pages:
+        tables.append(perm[k:k + m])
+        k += m
+    return plan, units, pool, tables
+
+
+def long_query(torch, wl, seed):
+    """The batch's q [B, QL, H, 576] bf16, identical on every rank (the pieces of one sequence
+    on different ranks attend the same query)."""
+    g = torch.Generator().manual_seed(seed + 7)
+    return torch.randn(len(wl["lens"]), wl["QL"], wl["H"], 576, generator=g).to(torch.bfloat16)
+
+
+def long_check(rt, torch, wl, dev, world, merged, seed, sm):
+    """Rank 0, after timing: rebuild every rank's pool, lay each sequence's pages end to end in
+    one pool, decode the whole batch unpartitioned in one call and compare it with the
+    partitioned result merged across the ranks (``merged``, [B, QL, H, 512]).  The pieces and
+    the whole sequences accumulate in different orders, so the gate is the attention tolerance
+    (2e-2 rel / 1e-2 abs elementwise), with the largest difference and the relative L2 reported."""
+    pools, seq_pages, base = [], [[] for _ in wl["lens"]], 0
+    for r in range(world):
+        _, units, pool, tables = long_rank_pool(rt, torch, wl, dev, r, world, seed)
+        for u, t in zip(units, tables):
+            seq_pages[u.seq].append((u.start, t.to(torch.int64) + base))
+        pools.append(pool)
+        base += pool.shape[0]
+    full = torch.cat(pools)
+    del pools
+    width = max(sum(t.numel() for _, t in sp) for sp in seq_pages)
+    tb = torch.full((len(wl["lens"]), width), -1, dtype=torch.int32)
+    for s, sp in enumerate(seq_pages):
+        t = torch.cat([t for _, t in sorted(sp, key=lambda x: x[0])])
+        tb[s, :t.numel()] = t.to(torch.int32)
+    sl = torch.tensor(wl["lens"], dtype=torch.int32, device=dev)
+    q = long_query(torch, wl, seed).to(dev)
+    ref = rt.mla_decode(q, full, None, 128, 512, 64, tb.to(dev), sl, max(wl["lens"]), bmm1_scale=sm)
+    torch.cuda.synchronize()
+    got, want = merged.float(), ref.float()
+    diff = (got - want).abs()
+    within = bool((diff <= 1e-2 + 2e-2 * want.abs()).all())
+    rel = float(torch.linalg.vector_norm(got - want) / torch.linalg.vector_norm(want))
+    del full
+    torch.cuda.empty_cache()
+    return {"merged_vs_unpartitioned": {"max_abs_diff": round(float(diff.max()), 6), "rel_l2": round(rel, 7),
+                                        "within_tol": within, "ranks": world}, "passed": within and rel < 1e-2}
+
+
 def make_long_step(rt, torch, wl, dev, rank, world, seed):
     """The partitioned long-context step on this rank: its pieces' pages written by the append
     kernel into a rank-local pool, two decode calls (pieces before a sequence's causal tail
@@ -246,21 +322,8 @@ def make_long_step(rt, torch, wl, dev, rank, world, seed):
     from glm53_flash_dual_dgx_spark_b200 import partition as P
 
     lens, QL, H = wl["lens"], wl["QL"], wl["H"]
-    plan = P.plan(lens, world * LONG_PIECES_PER_RANK, 64, q_len=QL)
-    units = [u for part in plan[rank * LONG_PIECES_PER_RANK:(rank + 1) * LONG_PIECES_PER_RANK] for u in part]
-    pages = [(u.tokens + 63) // 64 for u in units]
-    pool = torch.empty(sum(pages), 64, NV_BYTES, dtype=torch.uint8, device=dev)
-    torch.manual_seed(seed)
-    for c in range(0, pool.shape[0] * 64, 1 << 20):
-        n = min(1 << 20, pool.shape[0] * 64 - c)
-        rt.write_nvfp4(torch.randn(n, 512, device=dev).to(torch.bfloat16), pool, torch.arange(c, c + n, device=dev))
-    g = torch.Generator().manual_seed(seed)
-    perm = torch.randperm(pool.shape[0], generator=g).to(torch.int32)
-    tables, k = [], 0
-    for m in pages:
-        tables.append(perm[k:k + m])
-        k += m
-    q = torch.randn(len(lens), QL, H, 576, generator=g).to(torch.bfloat16).to(dev)
+    plan, units, pool, tables = long_rank_pool(rt, torch, wl, dev, rank, world, seed)
+    q = long_query(torch, wl, seed).to(dev)
     calls = []
     for last in (False, True):
         idx = [i for i, u in enumerate(units) if u.last == last]
@@ -814,6 +877,141 @@ def run_prefill(args, wl, rt, torch, dist, dev, rank, world, local):
         sys.exit("result check failed: a prefill output is outside 2e-2 rel / 1e-2 abs")
 
 
+def run_dsa(args, wl, rt, torch, dist, dev, rank, world, local):
+    """--workload dsa: the indexer's top-k over NVFP4 indexer keys, then the sparse decode, per
+    layer (weak scaling: 16 sequences and their pools per rank)."""
+    B, H, ctx, K = wl["B"], wl["H"], wl["ctx"], wl["topk"]
+    pages = B * ctx // 64
+    sm = 1.0 / math.sqrt(576)
+    layers = []
+    g = torch.Generator().manual_seed(1 + rank)
+    for li in range(2):                                 # 2 x (604 + 151) MB: well past the L2
+        pool = torch.empty(pages, 64, NV_BYTES, dtype=torch.uint8, device=dev)
+        index = torch.empty(pages, 64, INDEX_ROW_BYTES, dtype=torch.uint8, device=dev)
+        torch.manual_seed(1000 * (1 + rank) + li)
+        for c in range(0, pages * 64, 1 << 20):
+            n = min(1 << 20, pages * 64 - c)
+            slots = torch.arange(c, c + n, device=dev)
+            rt.write_nvfp4(torch.randn(n, 512, device=dev).to(torch.bfloat16), pool, slots)
+            rt.index_append(torch.randn(n, 128, device=dev).to(torch.bfloat16), index, slots)
+        tables = torch.randperm(pages, generator=g).view(B, ctx // 64).to(torch.int32).to(dev)
+        layers.append(dict(pool=pool, index=index, tables=tables,
+                           iq=torch.randn(B, 64, 128, generator=g).to(torch.bfloat16).to(dev),
+                           iw=(torch.rand(B, 64, generator=g) / 64).to(dev),
+                           q=torch.randn(B, 1, H, 576, generator=g).to(torch.bfloat16).to(dev),
+                           seq=torch.full((B,), ctx, dtype=torch.int32, device=dev),
+                           rows=torch.empty(B, K, dtype=torch.int32, device=dev),
+                           count=torch.empty(B, dtype=torch.int32, device=dev),
+                           out=torch.empty(B, 1, H, 512, dtype=torch.bfloat16, device=dev)))
+
+    def select(ly):
+        rt.index_topk(ly["iq"], ly["iw"], ly["index"], ly["tables"], ly["seq"], ctx, K,
+                      out_rows=ly["rows"], out_count=ly["count"])
+
+    def decode(ly):
+        rt.mla_decode(ly["q"], ly["pool"], None, 128, 512, 64, ly["rows"].view(B, 1, K), ly["count"], K,
+                      sparse_mla_top_k=K, out=ly["out"], bmm1_scale=sm)
+
+    for ly in layers:
+        select(ly)
+        decode(ly)
+    torch.cuda.synchronize()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    graphs = []
+    with torch.cuda.stream(st):
+        for ly in layers:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=st):
+                select(ly)
+                decode(ly)
+            graphs.append(gr)
+    torch.cuda.current_stream().wait_stream(st)
+    torch.cuda.synchronize()
+    steps = args.steps if args.steps_given else 500
+    sampler = ClockSampler(local)
+    sampler.start()
+    soak_end = time.perf_counter() + 1.0
+    k = 0
+    while time.perf_counter() < soak_end or k < args.warmup:
+        graphs[k % 2].replay()
+        k += 1
+        if k % 32 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for k in range(steps):
+        graphs[k % 2].replay()
+    ev1.record()
+    ev1.synchronize()
+    t1 = time.perf_counter()
+    if world > 1:
+        dist.barrier()
+    sampler.stop()
+    t_max = torch.tensor([ev0.elapsed_time(ev1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    per_ms = float(t_max.item()) / steps
+    kvb = kv_bytes_per_step(wl)
+    value = kvb * world / (per_ms / 1e3) / 1e9
+    # the two halves alone (eager, events around each)
+    sel_ms, dec_ms = [], []
+    for k in range(20):
+        ly = layers[k % 2]
+        a, b_, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        a.record()
+        select(ly)
+        b_.record()
+        decode(ly)
+        c.record()
+        c.synchronize()
+        sel_ms.append(a.elapsed_time(b_))
+        dec_ms.append(b_.elapsed_time(c))
+    sel_us = statistics.median(sel_ms) * 1e3
+    dec_us = statistics.median(dec_ms) * 1e3
+    # the decode of layer 0 against the exact attention over the rows the indexer picked
+    ly = layers[0]
+    check = prefill_check(torch, rt, dict(pool=ly["pool"], tables=ly["rows"].view(B, 1, K), q=ly["q"],
+                                          out=ly["out"]), [0, B - 1], sm)
+    errors = rt.device_errors(dev)
+    if rank == 0:
+        peak, peak_kind = load_peaks()
+        index_bytes = B * ctx * INDEX_ROW_BYTES
+        line = {
+            "metric": METRIC + " (indexer + sparse decode)", "value": round(value, 2), "unit": "GB/s",
+            "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16/f16",
+            "data": "synthetic (seeded N(0,1) latent and indexer keys quantised by the append kernels; N(0,1) q)",
+            "config": {"workload": wl["desc"], "global_batch": B * world, "seq_len": ctx, "topk": K,
+                       "index_heads": 64, "index_dim": 128,
+                       "l2": f"inputs larger than L2: 2 layers x {kvb / 2**20:.0f} MiB read per step",
+                       "parallelism": f"sequence-partitioned x{world} (weak scaling)"},
+            "bytes_per_step": {"index_keys": index_bytes, "latent_rows": B * K * NV_BYTES},
+            "decode_tokens_per_s": round(B * world / (per_ms / 1e3), 1),
+            "roofline": {"bound": "hbm", "achieved": round(index_bytes / (sel_us / 1e6) / 1e9, 2), "peak": peak,
+                         "unit": "GB/s", "frac": round(index_bytes / (sel_us / 1e6) / 1e9 / peak, 4),
+                         "peak_kind": peak_kind, "kernel": "index_score_kernel + index_topk_kernel",
+                         "per_launch_bytes": index_bytes, "kernel_ms": round(sel_us / 1e3, 5),
+                         "traffic": profile_traffic("dsa"), "decode_us": round(dec_us, 2),
+                         "step_frac_in_kernel": round(sel_us / 1e3 / per_ms, 3)},
+            "gpu_launches": steps * 5,
+            "clocks": sampler.summary(t0, t1),
+            "result_check": check,
+            "device_errors": errors,
+        }
+        print(json.dumps(line), flush=True)
+    del graphs
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if not check["passed"]:
+        sys.exit("result check failed: a decode output is outside 2e-2 rel / 1e-2 abs")
+
+
 def run_long(args, wl, rt, torch, dist, dev, rank, world, local):
     """--workload long: the partitioned config-4 layer (strong scaling)."""
     from glm53_flash_dual_dgx_spark_b200 import partition as P
@@ -904,12 +1102,22 @@ def run_long(args, wl, rt, torch, dist, dev, rank, world, local):
         dist.all_reduce(k_ms, op=dist.ReduceOp.MAX)
     kernel_ms = float(k_ms.item())
 
-    # after timing: the cross-rank merge (the only data collective)
+    # after timing: the cross-rank merge (the only data collective), then rank 0 checks the
+    # merged result against the unpartitioned decode of the same sequences
+    step()
+    torch.cuda.synchronize()
     if world > 1:
         out_u, lse_u = st["out_u"], st["lse_u"]
-        P.gather_merge(out_u, lse_u, [[u for part in st["plan"][r * LONG_PIECES_PER_RANK:(r + 1) * LONG_PIECES_PER_RANK]
-                                       for u in part] for r in range(world)], rank, wl["B"])
+        merged, _ = P.gather_merge(out_u, lse_u, [[u for part in st["plan"][r * LONG_PIECES_PER_RANK:(r + 1) * LONG_PIECES_PER_RANK]
+                                                  for u in part] for r in range(world)], rank, wl["B"])
         torch.cuda.synchronize()
+    else:
+        merged = st["out"]
+    check = long_check(rt, torch, wl, dev, world, merged, 1, sm) if rank == 0 else {"passed": True}
+    flag = torch.tensor([1 if check["passed"] else 0], dtype=torch.int32, device=dev)
+    if world > 1:
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    passed = bool(flag.item())
     errors = rt.device_errors(dev)
     if rank == 0:
         peak, peak_kind = load_peaks()
@@ -936,6 +1144,7 @@ def run_long(args, wl, rt, torch, dist, dev, rank, world, local):
                     "d2h_bytes_per_step": out_h.numel() * 2, "steps": e_steps},
             "gpu_launches": args.steps * launches,
             "clocks": sampler.summary(t0, t1),
+            "result_check": check,
             "device_errors": errors,
         }
         if world == 1:
@@ -949,6 +1158,8 @@ def run_long(args, wl, rt, torch, dist, dev, rank, world, local):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if not passed:
+        sys.exit("long: the merged partitioned result differs from the unpartitioned decode")
 
 
 # ---------------------------------------------------------------------------- CPU side
@@ -1340,6 +1551,9 @@ def main() -> None:
         return
     if wl.get("prefill"):
         run_prefill(args, wl, rt, torch, dist, dev, rank, world, local)
+        return
+    if wl.get("dsa"):
+        run_dsa(args, wl, rt, torch, dist, dev, rank, world, local)
         return
     if wl.get("dedup"):
         run_dedup(args, wl, rt, torch, dist, dev, rank, world, local)

@@ -13,11 +13,11 @@
 // for every visible position s < seq_len[b], then the topk largest.
 //
 // Kernels:
-//   index_score_kernel  one block per (query, 128-position tile): keys dequantised exactly
+//   index_score_kernel  one block per (query, run of 8 128-position tiles): keys dequantised exactly
 //                       to bf16 in shared memory (code x e4m3 scale has at most 5
 //                       significant bits), K . Q^T on the tensor cores (wmma bf16, fp32
 //                       accumulation), then the ReLU-weighted head sum per position.
-//   index_topk_kernel   one block per query: a 4-pass 8-bit radix select of the k-th largest
+//   index_topk_kernel   one block per query: an 8-pass 4-bit radix select of the k-th largest
 //                       score, then the selected positions written in ascending order (ties
 //                       at the threshold go to the lowest positions), mapped to pool rows.
 #include <mma.h>
@@ -32,7 +32,12 @@ constexpr int kITile = 128;                         // positions per score block
 constexpr int kIHeads = 64;                         // indexer heads
 constexpr int kIDim = NVFP4KV_INDEX_DIM;            // 128
 constexpr int kIRow = NVFP4KV_INDEX_ROW_BYTES;      // 72
-constexpr int kScoreSmem = kIHeads * kIDim * 2 + kITile * kIDim * 2 + kITile * kIHeads * 4;   // 81920
+// Shared-memory row strides padded by 16 bytes: rows 256 bytes apart would put every row of a
+// 16 x 16 fragment load in the same banks.
+constexpr int kQLd = kIDim + 8;                     // bf16 elements
+constexpr int kKLd = kIDim + 8;
+constexpr int kSLd = kIHeads + 4;                   // fp32 elements
+constexpr int kScoreSmem = kIHeads * kQLd * 2 + kITile * kKLd * 2 + kITile * kSLd * 4;   // 87040
 
 struct ScoreParams {
     const __nv_bfloat16* q;       // [batch][heads][128], row strides below
@@ -71,75 +76,110 @@ __device__ __forceinline__ float e2m1_val(uint32_t c) {
     return (c & 8u) ? -v : v;
 }
 
+// One thread's share of a key tile: position tid >> 1, half tid & 1 (64 elements = 4 blocks):
+// 32 code bytes and 4 scale bytes, loaded ahead of their use.
+struct KeyPart {
+    uint2 c[4];
+    uint32_t s;
+    bool ok;
+};
+
+__device__ __forceinline__ KeyPart load_key_part(const ScoreParams& p, int b, int pos, int L, int half) {
+    KeyPart k{};
+    const int64_t row = pos < L ? index_row(p.tables, p.tables_stride, b, pos, p.page_shift, p.num_pages) : -1;
+    k.ok = row >= 0;
+    if (k.ok) {
+        const uint8_t* src = p.pool + row * kIRow;
+#pragma unroll
+        for (int blk = 0; blk < 4; ++blk) k.c[blk] = *reinterpret_cast<const uint2*>(src + 32 * half + 8 * blk);
+        k.s = *reinterpret_cast<const uint32_t*>(src + 64 + 4 * half);
+    }
+    return k;
+}
+
+// Dequantise a key part into the bf16 tile row (code x scale is exact in bf16: at most 5
+// significant bits), zeros for a masked position.
+__device__ __forceinline__ void store_key_part(const KeyPart& k, uint32_t* dst) {
+    if (!k.ok) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) dst[j] = 0u;
+        return;
+    }
+#pragma unroll
+    for (int blk = 0; blk < 4; ++blk) {
+        const float s = e4m3_to_f32(static_cast<uint8_t>(k.s >> (8 * blk)));
+        const uint32_t w2[2] = {k.c[blk].x, k.c[blk].y};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t byte = (w2[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+            const __nv_bfloat162 v = __floats2bfloat162_rn(e2m1_val(byte & 15u) * s, e2m1_val(byte >> 4) * s);
+            dst[8 * blk + j] = *reinterpret_cast<const uint32_t*>(&v);
+        }
+    }
+}
+
+// Block = (entry b, a run of kTilesPerBlock position tiles): the entry's q and weights are
+// loaded once, and each tile's key bytes are loaded a tile ahead of their dequantisation.
+constexpr int kTilesPerBlock = 8;
+
 __global__ void __launch_bounds__(256) index_score_kernel(const ScoreParams p, int32_t* err) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem);              // [64 heads][128]
-    __nv_bfloat16* ks = qs + kIHeads * kIDim;                                 // [128 positions][128]
-    float* ss = reinterpret_cast<float*>(ks + kITile * kIDim);                // [128 positions][64 heads]
+    __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem);              // [64 heads][kQLd]
+    __nv_bfloat16* ks = qs + kIHeads * kQLd;                                  // [128 positions][kKLd]
+    float* ss = reinterpret_cast<float*>(ks + kITile * kKLd);                 // [128 positions][kSLd]
     __shared__ float ws[kIHeads];
-    const int b = blockIdx.x / p.tiles, tile = blockIdx.x % p.tiles;
+    const int runs = (p.tiles + kTilesPerBlock - 1) / kTilesPerBlock;
+    const int b = blockIdx.x / runs, run = blockIdx.x % runs;
     const int L = clamp_len(p.seq_lens, b, p.max_seq_len, err);
-    if (tile * kITile >= L) return;                  // the whole block: nothing visible here
-    const int tid = threadIdx.x;
+    const int t0 = run * kTilesPerBlock;
+    const int t1 = min(min(t0 + kTilesPerBlock, p.tiles), (L + kITile - 1) / kITile);
+    if (t0 >= t1) return;                            // the whole block: nothing visible here
+    const int tid = threadIdx.x, warp = tid >> 5;
     for (int i = tid; i < kIHeads * kIDim / 8; i += blockDim.x) {
         const int h = i >> 4, c = i & 15;
-        reinterpret_cast<uint4*>(qs)[i] = ldg_nc_v4(p.q + b * p.q_sb + h * p.q_sh + 8 * c);
+        *reinterpret_cast<uint4*>(qs + h * kQLd + 8 * c) = ldg_nc_v4(p.q + b * p.q_sb + h * p.q_sh + 8 * c);
     }
     if (tid < kIHeads) ws[tid] = __ldg(p.w + b * p.w_sb + tid);
-    // keys: thread (position tid >> 1, half tid & 1) dequantises 64 elements = 4 blocks
     const int tok = tid >> 1, half = tid & 1;
-    const int pos = tile * kITile + tok;
-    const int64_t row = pos < L ? index_row(p.tables, p.tables_stride, b, pos, p.page_shift, p.num_pages) : -1;
-    uint32_t* kdst = reinterpret_cast<uint32_t*>(ks + tok * kIDim + 64 * half);
-    if (row >= 0 && row < p.pool_rows) {
-        const uint8_t* src = p.pool + row * kIRow;
-        const uint32_t sw = *reinterpret_cast<const uint32_t*>(src + 64 + 4 * half);   // 4 scale bytes
+    uint32_t* kdst = reinterpret_cast<uint32_t*>(ks + tok * kKLd + 64 * half);
+    KeyPart next = load_key_part(p, b, t0 * kITile + tok, L, half);
+    using namespace nvcuda;
+#pragma unroll 1
+    for (int tile = t0; tile < t1; ++tile) {
+        const KeyPart cur = next;
+        __syncthreads();                             // the previous tile's keys are consumed
+        store_key_part(cur, kdst);
+        if (tile + 1 < t1) next = load_key_part(p, b, (tile + 1) * kITile + tok, L, half);
+        __syncthreads();
+        // warp w: positions 16w .. 16w+15 against all 64 heads
+        wmma::fragment<wmma::accumulator, 16, 16, 16, float> acc[4];
 #pragma unroll
-        for (int blk = 0; blk < 4; ++blk) {
-            const uint2 cw = *reinterpret_cast<const uint2*>(src + 32 * half + 8 * blk);
-            const float s = e4m3_to_f32(static_cast<uint8_t>(sw >> (8 * blk)));
-            const uint32_t w2[2] = {cw.x, cw.y};
+        for (int n = 0; n < 4; ++n) wmma::fill_fragment(acc[n], 0.0f);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const uint32_t byte = (w2[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-                // code x scale is exact in bf16 (at most 5 significant bits)
-                const __nv_bfloat162 v = __floats2bfloat162_rn(e2m1_val(byte & 15u) * s, e2m1_val(byte >> 4) * s);
-                kdst[8 * blk + j] = *reinterpret_cast<const uint32_t*>(&v);
+        for (int kk = 0; kk < kIDim / 16; ++kk) {
+            wmma::fragment<wmma::matrix_a, 16, 16, 16, __nv_bfloat16, wmma::row_major> a;
+            wmma::load_matrix_sync(a, ks + 16 * warp * kKLd + 16 * kk, kKLd);
+#pragma unroll
+            for (int n = 0; n < 4; ++n) {
+                wmma::fragment<wmma::matrix_b, 16, 16, 16, __nv_bfloat16, wmma::col_major> bq;
+                wmma::load_matrix_sync(bq, qs + 16 * n * kQLd + 16 * kk, kQLd);
+                wmma::mma_sync(acc[n], a, bq, acc[n]);
             }
         }
-    } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) kdst[j] = 0u;
-    }
-    __syncthreads();
-    // warp w: positions 16w .. 16w+15 against all 64 heads
-    const int warp = tid >> 5;
-    using namespace nvcuda;
-    wmma::fragment<wmma::accumulator, 16, 16, 16, float> acc[4];
-#pragma unroll
-    for (int n = 0; n < 4; ++n) wmma::fill_fragment(acc[n], 0.0f);
-#pragma unroll
-    for (int kk = 0; kk < kIDim / 16; ++kk) {
-        wmma::fragment<wmma::matrix_a, 16, 16, 16, __nv_bfloat16, wmma::row_major> a;
-        wmma::load_matrix_sync(a, ks + 16 * warp * kIDim + 16 * kk, kIDim);
-#pragma unroll
-        for (int n = 0; n < 4; ++n) {
-            wmma::fragment<wmma::matrix_b, 16, 16, 16, __nv_bfloat16, wmma::col_major> bq;
-            wmma::load_matrix_sync(bq, qs + 16 * n * kIDim + 16 * kk, kIDim);
-            wmma::mma_sync(acc[n], a, bq, acc[n]);
-        }
-    }
-#pragma unroll
-    for (int n = 0; n < 4; ++n)
-        wmma::store_matrix_sync(ss + 16 * warp * kIHeads + 16 * n, acc[n], kIHeads, wmma::mem_row_major);
-    __syncwarp();
-    // thread (position tid >> 1, heads 32 half .. +32): the ReLU-weighted sum, halves combined
-    float sum = 0.0f;
+        for (int n = 0; n < 4; ++n)
+            wmma::store_matrix_sync(ss + 16 * warp * kSLd + 16 * n, acc[n], kSLd, wmma::mem_row_major);
+        __syncwarp();
+        // thread (position tid >> 1, heads 32 half .. +32): the ReLU-weighted sum, halves combined
+        float sum = 0.0f;
 #pragma unroll 8
-    for (int h = 0; h < 32; ++h) sum = fmaf(ws[32 * half + h], fmaxf(ss[tok * kIHeads + 32 * half + h], 0.0f), sum);
-    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
-    if (half == 0 && pos < L)
-        p.scores[static_cast<int64_t>(b) * p.tiles * kITile + pos] = row >= 0 ? sum : -INFINITY;
+        for (int h = 0; h < 32; ++h)
+            sum = fmaf(ws[32 * half + h], fmaxf(ss[tok * kSLd + 32 * half + h], 0.0f), sum);
+        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+        const int pos = tile * kITile + tok;
+        if (half == 0 && pos < L)
+            p.scores[static_cast<int64_t>(b) * p.tiles * kITile + pos] = cur.ok ? sum : -INFINITY;
+    }
 }
 
 // ------------------------------------------------------------------ top-k selection
@@ -149,33 +189,6 @@ constexpr int kKThreads = 1024;
 __device__ __forceinline__ uint32_t score_key(float f) {
     const uint32_t u = __float_as_uint(f);
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
-// Block-wide exclusive scan of one value per thread (1024 threads); `total` gets the sum.
-__device__ __forceinline__ int block_scan_1024(int v, int* warp_sums, int& total) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int x = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xFFFFFFFFu, x, o);
-        if (lane >= o) x += y;
-    }
-    if (lane == 31) warp_sums[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-        int w = warp_sums[lane];
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xFFFFFFFFu, w, o);
-            if (lane >= o) w += y;
-        }
-        warp_sums[lane] = w;
-    }
-    __syncthreads();
-    total = warp_sums[31];
-    const int before = warp == 0 ? 0 : warp_sums[warp - 1];
-    __syncthreads();
-    return before + x - v;
 }
 
 struct TopkParams {
@@ -191,8 +204,7 @@ struct TopkParams {
 };
 
 __global__ void __launch_bounds__(kKThreads) index_topk_kernel(const TopkParams p, int32_t* err) {
-    __shared__ int hist[32][257];                   // per-warp 256-bin histograms (+1 pad)
-    __shared__ int warp_sums[32];
+    __shared__ int hist[32][17];                    // per-warp counts of the 16 digits
     __shared__ uint32_t s_prefix, s_mask;
     __shared__ int s_remaining;
     const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -209,45 +221,47 @@ __global__ void __launch_bounds__(kKThreads) index_topk_kernel(const TopkParams 
             s_mask = 0u;
             s_remaining = k;
         }
-        for (int shift = 24; shift >= 0; shift -= 8) {
-            for (int i = tid; i < 32 * 257; i += kKThreads) (&hist[0][0])[i] = 0;
-            __syncthreads();
+        __syncthreads();
+        // 4-bit digits, most significant first: each thread counts the 16 digits of its
+        // candidates in registers (no shared-memory atomics: the scores crowd into a few bins,
+        // where atomics serialise), the warps reduce them, and warp 0 finds the digit at which
+        // the count from the top reaches the number still wanted
+        for (int shift = 28; shift >= 0; shift -= 4) {
             const uint32_t prefix = s_prefix, mask = s_mask;
+            int c[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) c[j] = 0;
             for (int pos = tid; pos < n; pos += kKThreads) {
                 const uint32_t u = score_key(sc[pos]);
-                if ((u & mask) == prefix) atomicAdd(&hist[warp][(u >> shift) & 255u], 1);
+                const uint32_t d = (u & mask) == prefix ? (u >> shift) & 15u : 16u;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) c[j] += d == static_cast<uint32_t>(j);
             }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) c[j] = __reduce_add_sync(0xFFFFFFFFu, c[j]);
+            if (lane == 0)
+#pragma unroll
+                for (int j = 0; j < 16; ++j) hist[warp][j] = c[j];
             __syncthreads();
             if (warp == 0) {
-                // bins 255 .. 0 in chunks of 32 from the top; find where the running count
-                // from the top reaches `remaining`
                 const int remaining = s_remaining;
-                int above = 0, found = -1, above_found = 0;
-                for (int base = 224; base >= 0 && found < 0; base -= 32) {
-                    const int bin = base + (31 - lane);      // lane 0 takes the highest bin
-                    int c = 0;
-                    for (int w = 0; w < 32; ++w) c += hist[w][bin];
-                    int incl = c;                            // inclusive prefix over lanes 0..lane
+                const int digit = 15 - lane;                 // lane 0: the highest digit
+                int cnt = 0;
+                if (lane < 16)
+                    for (int w = 0; w < 32; ++w) cnt += hist[w][digit];
+                int incl = cnt;
 #pragma unroll
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-                        if (lane >= o) incl += y;
-                    }
-                    const bool hit = above + incl >= remaining;
-                    const unsigned ballot = __ballot_sync(0xFFFFFFFFu, hit);
-                    if (ballot) {
-                        const int first = __ffs(ballot) - 1;
-                        const int excl = __shfl_sync(0xFFFFFFFFu, incl - c, first);
-                        found = base + (31 - first);
-                        above_found = above + excl;
-                    } else {
-                        above += __shfl_sync(0xFFFFFFFFu, incl, 31);
-                    }
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                    if (lane >= o) incl += y;
                 }
+                const unsigned hit = __ballot_sync(0xFFFFFFFFu, lane < 16 && incl >= remaining);
+                const int first = __ffs(hit) - 1;            // there always is one
+                const int above = __shfl_sync(0xFFFFFFFFu, incl - cnt, first);
                 if (lane == 0) {
-                    s_prefix |= static_cast<uint32_t>(found) << shift;
-                    s_mask |= 255u << shift;
-                    s_remaining = remaining - above_found;
+                    s_prefix |= static_cast<uint32_t>(15 - first) << shift;
+                    s_mask |= 15u << shift;
+                    s_remaining = remaining - above;
                 }
             }
             __syncthreads();
@@ -255,33 +269,48 @@ __global__ void __launch_bounds__(kKThreads) index_topk_kernel(const TopkParams 
         thr = s_prefix;
         need_eq = s_remaining;
     }
-    // selection in ascending position order: thread tid owns positions [tid c, tid c + c)
-    const int chunk = (n + kKThreads - 1) / kKThreads;
-    const int lo = tid * chunk, hi = min(n, lo + chunk);
-    int eq = 0;
-    if (k < n)
-        for (int pos = lo; pos < hi; ++pos) eq += score_key(sc[pos]) == thr;
-    int eq_total;
-    const int eq_base = block_scan_1024(eq, warp_sums, eq_total);
-    int sel = 0;
-    for (int pos = lo, r = eq_base; pos < hi; ++pos) {
-        if (k >= n) { ++sel; continue; }
-        const uint32_t u = score_key(sc[pos]);
-        if (u > thr) ++sel;
-        else if (u == thr) sel += (r++ < need_eq);
-    }
-    int sel_total;
-    int o = block_scan_1024(sel, warp_sums, sel_total);
-    for (int pos = lo, r = eq_base; pos < hi; ++pos) {
-        bool take = k >= n;
-        if (!take) {
-            const uint32_t u = score_key(sc[pos]);
-            take = u > thr || (u == thr && r++ < need_eq);
+    // selection in ascending position order, in coalesced rounds of 1024 positions: the rank of
+    // an equal-to-threshold position among the ties, and its output slot, are block prefix
+    // counts (warp ballots, then the warps' totals) carried from round to round
+    __shared__ int cnt[32];
+    int eq_before = 0, out_before = 0;
+    for (int base = 0; base < n; base += kKThreads) {
+        const int pos = base + tid;
+        const uint32_t u = pos < n ? score_key(sc[pos]) : 0u;
+        const bool all = k >= n;
+        const bool gt = pos < n && !all && u > thr;
+        const bool eq = pos < n && !all && u == thr;
+        const unsigned below = (1u << lane) - 1u;
+        // rank of this tie among the round's ties before it
+        const unsigned beq = __ballot_sync(0xFFFFFFFFu, eq);
+        if (lane == 0) cnt[warp] = __popc(beq);
+        __syncthreads();
+        int eq_off = 0, eq_round = 0;
+        for (int w = 0; w < 32; ++w) {
+            const int c = cnt[w];
+            eq_off += w < warp ? c : 0;
+            eq_round += c;
         }
-        if (take) {
+        __syncthreads();
+        const int rank = eq_before + eq_off + __popc(beq & below);
+        const bool take = (all && pos < n) || gt || (eq && rank < need_eq);
+        const unsigned btk = __ballot_sync(0xFFFFFFFFu, take);
+        if (lane == 0) cnt[warp] = __popc(btk);
+        __syncthreads();
+        int tk_off = 0, tk_round = 0;
+        for (int w = 0; w < 32; ++w) {
+            const int c = cnt[w];
+            tk_off += w < warp ? c : 0;
+            tk_round += c;
+        }
+        __syncthreads();
+        const int slot = out_before + tk_off + __popc(btk & below);
+        if (take && slot < p.topk) {   // exactly k are taken; the bound only guards the row
             const int64_t row = index_row(p.tables, p.tables_stride, b, pos, p.page_shift, p.num_pages);
-            out[o++] = row >= 0 ? static_cast<int32_t>(row) : -1;
+            out[slot] = row >= 0 ? static_cast<int32_t>(row) : -1;
         }
+        eq_before += eq_round;
+        out_before += tk_round;
     }
     for (int j = k + tid; j < p.topk; j += kKThreads) out[j] = -1;
 }
@@ -345,7 +374,8 @@ extern "C" int nvfp4kv_index_topk(const void* q, int64_t q_stride_b, int64_t q_s
         sp.tables = tables; sp.tables_stride = tables_stride; sp.seq_lens = seq_lens;
         sp.page_shift = shift; sp.max_seq_len = max_seq_len; sp.tiles = tiles;
         sp.scores = static_cast<float*>(workspace);
-        index_score_kernel<<<static_cast<unsigned>(static_cast<int64_t>(batch) * tiles), 256, kScoreSmem, st>>>(
+        const int64_t runs = (tiles + kTilesPerBlock - 1) / kTilesPerBlock;
+        index_score_kernel<<<static_cast<unsigned>(static_cast<int64_t>(batch) * runs), 256, kScoreSmem, st>>>(
             sp, err_flag);
         int rc = check_launch("nvfp4kv_index_topk (scores)");
         if (rc != NVFP4KV_OK) return rc;
