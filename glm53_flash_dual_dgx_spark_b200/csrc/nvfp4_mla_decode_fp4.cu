@@ -55,6 +55,7 @@ constexpr int kProducerWarp0 = 8;                 // warpgroup 2: V chunks and t
 constexpr int kProducerWarps = 4;
 constexpr int kMmaWarp = 12;                      // warpgroup 3: MMA issue,
 constexpr int kTmaWarp = 13;                      //   every TMA / bulk load, and two spare warps
+constexpr int kLoadBar = 2;                       // named barrier of the control warpgroup's shared loads
 constexpr int kThreads = 16 * 32;                 // 512
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
 constexpr uint32_t kRegsSoftmax = 168, kRegsProducer = 96, kRegsCtl = 80;
@@ -421,6 +422,60 @@ __device__ __forceinline__ void load_rows_gather4(const Fp4Params& p, const void
     tma_gather4(slot_base + kCodeBytes + r0 * 32, tm_scales, 256, rows, bar_full);
 }
 
+// The prepared Q image of (sequence b, query group g) -> shared memory: Q-term codes, their
+// scale image (in the P^T buffer until the set-up moves it to TMEM) and the per-row constants.
+// It is the output of the Q preparation kernel this one may overlap (all else this kernel reads
+// was complete before that kernel started), hence the grid dependency wait.
+template <int kQB, int kPT, int kQS>
+__device__ __forceinline__ void load_q_image(const Fp4Params& p, uint32_t sbase, uint32_t bar_q, int b, int g) {
+    griddep_wait();
+    const uint8_t* img = p.qimg + static_cast<size_t>(b * p.groups + g) * kQImageBytes;
+    mbar_arrive_expect_tx(bar_q, static_cast<uint32_t>(kQImageBytes));
+    bulk_copy_g2s(sbase + kQB, img, 2 * kCodeBytes, bar_q);
+    bulk_copy_g2s(sbase + kPT, img + 2 * kCodeBytes, 2 * 4096, bar_q);
+    bulk_copy_g2s(sbase + kQS, img + 2 * kCodeBytes + 2 * 4096, 256, bar_q);
+}
+
+// The same copy issued by the four warps of the control warpgroup together (the first ring
+// tiles, before the MMA warp has anything to issue): the issue of a gather4 serialises over
+// the lanes of a warp (measured: 128 rows take 3.6 us from one warp, 1.9 us from four), so
+// warp wq takes rows 32 wq .. 32 wq + 31, eight lanes of four rows, and writes mask word wq.
+// Warp 1 of the four arms the barrier once every word is written and before any copy issues.
+__device__ __forceinline__ void load_rows_gather4_x4(const Fp4Params& p, const void* tm_codes, const void* tm_scales,
+                                                     uint32_t slot_base, uint32_t bar_full, uint32_t* slot_mask,
+                                                     const int* sidx, int idx_base, int b, int tile_start, int end,
+                                                     int wq, int lane) {
+    int rows[4];
+    uint32_t live = 0;
+    const int r0 = 32 * wq + 4 * lane;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int pos = tile_start + r0 + j;
+        const int64_t row = lane < 8 && pos < end ? token_row<true>(p, sidx, true, idx_base, b, pos, true) : -1;
+        live |= static_cast<uint32_t>(row >= 0) << j;
+        rows[j] = row >= 0 ? static_cast<int>(row) : 0;
+    }
+    uint32_t bits[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) bits[j] = __ballot_sync(0xFFFFFFFFu, (live >> j) & 1u);
+    if (lane == 0) {   // row 32 wq + 4m + j is bit 4m + j of word wq
+        uint32_t w = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int m = 0; m < 8; ++m) w |= ((bits[j] >> m) & 1u) << (4 * m + j);
+        slot_mask[wq] = w;
+    }
+    named_bar_sync(kLoadBar, 128);   // every mask word written before the arming arrive
+    if (wq == 1 && lane == 0) mbar_arrive_expect_tx(bar_full, kSlotBytes);
+    named_bar_sync(kLoadBar, 128);   // armed before any copy of the phase issues
+    if (lane < 8) {
+        tma_gather4(slot_base + r0 * 128, tm_codes, 0, rows, bar_full);
+        tma_gather4(slot_base + 16384 + r0 * 128, tm_codes, 128, rows, bar_full);
+        tma_gather4(slot_base + kCodeBytes + r0 * 32, tm_scales, 256, rows, bar_full);
+    }
+}
+
 // Pool scales of the tile in `slot` -> TMEM scale-factor columns `col` of this warp's
 // sub-partition: column 4kk+q of lane r holds the 4 scales (dims 64kk..64kk+63) of token
 // 32q + r.  Every sub-partition needs a full copy.
@@ -537,6 +592,11 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
     constexpr int SM_QS = C::SM_QS, SM_LIM = C::SM_LIM, SM_LSUM = C::SM_LSUM, SM_RED = C::SM_RED;
     constexpr int SM_ROWOFF = C::SM_ROWOFF, SM_FLAGS = C::SM_FLAGS, SM_TMASK = C::SM_TMASK, SM_BARS = C::SM_BARS;
     constexpr int SM_IDX = C::SM_IDX;
+    // Short sparse splits (the two-slot ring: at most two tiles) have the control warpgroup
+    // write tile 1's pool scales into TMEM, each warp its sub-partition's copy (warps 12-15 are
+    // sub-partitions 0-3); on the softmax side that write sat between P(0) and QK(1).  Every
+    // other pool-scale write is the softmax warps'.
+    constexpr bool kSfaByCtl = kSparse && kSlots == 2;
     constexpr int B_FULL = C::B_FULL, B_FREE = C::B_FREE, B_QKD = C::B_QKD, B_SFA_FULL = C::B_SFA_FULL;
     constexpr int B_S_FULL = C::B_S_FULL, B_S_FREE = C::B_S_FREE, B_P_FULL = C::B_P_FULL, B_PV_DONE = C::B_PV_DONE;
     constexpr int B_V_FULL = C::B_V_FULL, B_V_EMPTY = C::B_V_EMPTY, B_Q = C::B_Q, B_DRAIN = C::B_DRAIN;
@@ -613,38 +673,43 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = static_cast<uint32_t>(flags[0]);
+    auto sfa1_by_ctl = [&]() {
+        mbar_wait(bar(B_FULL + 1), 0, abort_flag, p.err);
+        scales_to_tmem_narrow(smem + SM_STAGE + kSlotBytes + kCodeBytes,
+                              tmem + kTSFA + 32 + (static_cast<uint32_t>(32 * (warp & 3)) << 16), lane);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_SFA_FULL + 1));
+    };
     griddep_launch_dependents();   // the split combine may be scheduled; it waits for this grid
 
     if (warp >= kMmaWarp) {
     warpgroup_reg_dealloc<kRegsCtl>();
+    if constexpr (kSparse) {
+        // the first ring tiles: rows gathered by all four warps of the group
+        if (lane == 0) {
+            tma_prefetch_desc(&tm_codes);
+            tma_prefetch_desc(&tm_scales);
+        }
+        for (int j = 0; j < kSlots && j < n_tiles; ++j)
+            load_rows_gather4_x4(p, &tm_codes, &tm_scales, sbase + SM_STAGE + j * kSlotBytes, bar(B_FULL + j),
+                                 tmask + 4 * j, sidx, idx_base, b, start + j * kTile, end, warp - kMmaWarp, lane);
+        // the MMA warp writes its copy after QK(0) is issued
+        if (kSfaByCtl && warp != kMmaWarp && n_tiles > 1) sfa1_by_ctl();
+    }
     if (warp == kTmaWarp) {
         // ============================================================ TMA / bulk loads
-        // The Q image is the output of the Q preparation kernel this one may overlap (all else
-        // this kernel reads was complete before that kernel started).  Sparse: it is copied
-        // right after the first tile's row gather, which does not depend on it and takes the
-        // longer; dense: first (measured: the dense step lost 0.2 us the other way round).
-        auto load_q = [&]() {
-            griddep_wait();
-            const uint8_t* img = p.qimg + static_cast<size_t>(b * p.groups + g) * kQImageBytes;
-            mbar_arrive_expect_tx(bar(B_Q), static_cast<uint32_t>(kQImageBytes));
-            bulk_copy_g2s(sbase + SM_QB, img, 2 * kCodeBytes, bar(B_Q));
-            bulk_copy_g2s(sbase + SM_PT, img + 2 * kCodeBytes, 2 * 4096, bar(B_Q));
-            bulk_copy_g2s(sbase + SM_QS, img + 2 * kCodeBytes + 2 * 4096, 256, bar(B_Q));
-        };
+        // The Q image (the output of the Q preparation kernel this one may overlap) is copied
+        // first for dense (measured: the dense step lost 0.2 us the other way round); for
+        // sparse a softmax thread copies it while the row gathers issue.
         if (lane == 0) {
             tma_prefetch_desc(&tm_codes);
             tma_prefetch_desc(&tm_scales);
         }
         if constexpr (kSparse) {
-            // tile j -> slot j % kSlots once QK(j - kSlots) and the producers are done with it
-            int issued = 0;   // tiles issued; tile j completes phase j / kSlots of its slot
-            for (int j = 0; j < kSlots && j < n_tiles; ++j) {
-                load_rows_gather4(p, &tm_codes, &tm_scales, sbase + SM_STAGE + j * kSlotBytes, bar(B_FULL + j),
-                                  tmask + 4 * j, sidx, idx_base, b, start + j * kTile, end, lane);
-                issued = j + 1;
-                if (j == 0 && lane == 0) load_q();
-            }
-            if (n_tiles == 0 && lane == 0) load_q();
+            // tile j -> slot j % kSlots once QK(j - kSlots) and the producers are done with it;
+            // the first kSlots tiles were issued by the whole group above
+            int issued = n_tiles < kSlots ? n_tiles : kSlots;   // tile j completes phase j / kSlots of its slot
             // Splits longer than the index window: after tile t is issued, the rows of tile
             // t + kSlots are loaded into registers (window slot (t + kSlots) % kIdxTiles, whose
             // tile t + kSlots - kIdxTiles was issued long before) and stored before the next
@@ -685,7 +750,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             for (int j = issued > kSlots ? issued - kSlots : 0; j < issued; ++j)
                 mbar_drain_wait(bar(B_FULL + j % kSlots), (j / kSlots) & 1);
         } else if (lane == 0) {
-            load_q();
+            load_q_image<SM_QB, SM_PT, SM_QS>(p, sbase, bar(B_Q), b, g);
             int issued = 0;   // tiles loaded; tile j completes phase j / kSlots of slot j % kSlots
             for (int j = 0; j < kSlots && j < n_tiles; ++j) {
                 load_tile(p, &tm_codes, &tm_scales, sbase, bar(B_FULL + j), sidx, staged, idx_base, b,
@@ -723,6 +788,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
         for (int i = 0; i <= n_tiles; ++i) {
             if (i < n_tiles) {
                 const int slot = i % kSlots, fb = i & 1;
+                if (kSfaByCtl && i == 1) sfa1_by_ctl();
                 mbar_wait(bar(B_FULL + slot), (i / kSlots) & 1, abort_flag, p.err);
                 mbar_wait(bar(B_SFA_FULL + fb), (i >> 1) & 1, abort_flag, p.err);
                 if (i > 0) mbar_wait(bar(B_S_FREE), (i - 1) & 1, abort_flag, p.err);
@@ -850,6 +916,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
 
         // ---- set-up: per-row constants, Q-term scales (B scale factors) and tile 0's pool
         // scales (A scale factors) into TMEM; every sub-partition gets a full copy
+        if (kSparse && threadIdx.x == 0) load_q_image<SM_QB, SM_PT, SM_QS>(p, sbase, bar(B_Q), b, g);
         mbar_wait(bar(B_Q), 0, abort_flag, p.err);
         if (threadIdx.x < kNQ) {
             const int n = threadIdx.x;
@@ -894,7 +961,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             // P(i) is computed.  Short sparse splits (one or two tiles, the two-slot ring) start
             // with both tiles' row gathers in flight: there they go after P(i), which must not
             // wait for tile i+1 to land.
-            const bool next_tile = hh == 0 && i + 1 < n_tiles;
+            const bool next_tile = hh == 0 && i + 1 < n_tiles && !(kSfaByCtl && i == 0);
             const bool early = next_tile && !(kSparse && kSlots == 2);
             if (early) {
                 mbar_wait(bar(B_FULL + (i + 1) % kSlots), ((i + 1) / kSlots) & 1, abort_flag, p.err);
