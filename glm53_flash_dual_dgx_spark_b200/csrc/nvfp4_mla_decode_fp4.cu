@@ -104,7 +104,8 @@ struct DecCfg {
     static constexpr int B_V_EMPTY = B_V_FULL + V;      // [V] PV finished reading the V chunk
     static constexpr int B_Q = B_V_EMPTY + V;           // prepared Q landed (set-up)
     static constexpr int B_DRAIN = B_Q + 1;             // every MMA of the CTA complete (before TMEM is freed)
-    static constexpr int kNumBars = B_DRAIN + 1;
+    static constexpr int B_SFB = B_DRAIN + 1;           // Q-term scales (B scale factors) in TMEM
+    static constexpr int kNumBars = B_SFB + 1;
     static constexpr int SM_IDX = SM_BARS + ((kNumBars * 8 + 15) / 16) * 16;
     static constexpr int SM_END = SM_IDX + kMaxIdx * 4;
     static constexpr int kSmemBytes = SM_END + 1024;                 // slack to align the base
@@ -592,14 +593,15 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
     constexpr int SM_QS = C::SM_QS, SM_LIM = C::SM_LIM, SM_LSUM = C::SM_LSUM, SM_RED = C::SM_RED;
     constexpr int SM_ROWOFF = C::SM_ROWOFF, SM_FLAGS = C::SM_FLAGS, SM_TMASK = C::SM_TMASK, SM_BARS = C::SM_BARS;
     constexpr int SM_IDX = C::SM_IDX;
-    // Short sparse splits (the two-slot ring: at most two tiles) have the control warpgroup
-    // write tile 1's pool scales into TMEM, each warp its sub-partition's copy (warps 12-15 are
-    // sub-partitions 0-3); on the softmax side that write sat between P(0) and QK(1).  Every
-    // other pool-scale write is the softmax warps'.
-    constexpr bool kSfaByCtl = kSparse && kSlots == 2;
+    // Sparse: the control warpgroup writes tiles 0 and 1's pool scales into TMEM (their slots'
+    // first use), each warp its sub-partition's copy (warps 12-15 are sub-partitions 0-3), as
+    // the tiles land; on the softmax side tile 0's waited for the Q image and tile 1's sat
+    // between P(0) and QK(1).  Every later pool-scale write is the softmax warps'.
+    constexpr bool kSfaByCtl = kSparse;
     constexpr int B_FULL = C::B_FULL, B_FREE = C::B_FREE, B_QKD = C::B_QKD, B_SFA_FULL = C::B_SFA_FULL;
     constexpr int B_S_FULL = C::B_S_FULL, B_S_FREE = C::B_S_FREE, B_P_FULL = C::B_P_FULL, B_PV_DONE = C::B_PV_DONE;
     constexpr int B_V_FULL = C::B_V_FULL, B_V_EMPTY = C::B_V_EMPTY, B_Q = C::B_Q, B_DRAIN = C::B_DRAIN;
+    constexpr int B_SFB = C::B_SFB;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -652,6 +654,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
         mbar_init(bar(B_P_FULL), kSoftmaxWarps);
         mbar_init(bar(B_PV_DONE), 1);
         mbar_init(bar(B_Q), 1);
+        mbar_init(bar(B_SFB), kSoftmaxWarps);
         mbar_init(bar(B_DRAIN), 1);
         flags[1] = 0;
         mbar_fence_init();
@@ -673,13 +676,13 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = static_cast<uint32_t>(flags[0]);
-    auto sfa1_by_ctl = [&]() {
-        mbar_wait(bar(B_FULL + 1), 0, abort_flag, p.err);
-        scales_to_tmem_narrow(smem + SM_STAGE + kSlotBytes + kCodeBytes,
-                              tmem + kTSFA + 32 + (static_cast<uint32_t>(32 * (warp & 3)) << 16), lane);
+    auto sfa_by_ctl = [&](int j) {   // tile j < 2: ring slot j, TMEM scale slot j
+        mbar_wait(bar(B_FULL + j), 0, abort_flag, p.err);
+        scales_to_tmem_narrow(smem + SM_STAGE + j * kSlotBytes + kCodeBytes,
+                              tmem + kTSFA + 32 * j + (static_cast<uint32_t>(32 * (warp & 3)) << 16), lane);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_SFA_FULL + 1));
+        if (lane == 0) mbar_arrive(bar(B_SFA_FULL + j));
     };
     griddep_launch_dependents();   // the split combine may be scheduled; it waits for this grid
 
@@ -694,8 +697,9 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
         for (int j = 0; j < kSlots && j < n_tiles; ++j)
             load_rows_gather4_x4(p, &tm_codes, &tm_scales, sbase + SM_STAGE + j * kSlotBytes, bar(B_FULL + j),
                                  tmask + 4 * j, sidx, idx_base, b, start + j * kTile, end, warp - kMmaWarp, lane);
-        // the MMA warp writes its copy after QK(0) is issued
-        if (kSfaByCtl && warp != kMmaWarp && n_tiles > 1) sfa1_by_ctl();
+        // the MMA warp writes its copies in its loop, just before it waits for them
+        if (kSfaByCtl && warp != kMmaWarp)
+            for (int j = 0; j < 2 && j < n_tiles; ++j) sfa_by_ctl(j);
     }
     if (warp == kTmaWarp) {
         // ============================================================ TMA / bulk loads
@@ -784,11 +788,12 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
         const uint64_t dq0 = smem_desc_sw128(sbase + SM_QB, 16, 1024);
         const uint64_t dpt = smem_desc_sw128(sbase + SM_PT, 16, 1024);
         mbar_wait(bar(B_Q), 0, abort_flag, p.err);   // Q-term codes in shared memory
+        mbar_wait(bar(B_SFB), 0, abort_flag, p.err); // and their scales in TMEM (both passes)
 #pragma unroll 1
         for (int i = 0; i <= n_tiles; ++i) {
             if (i < n_tiles) {
                 const int slot = i % kSlots, fb = i & 1;
-                if (kSfaByCtl && i == 1) sfa1_by_ctl();
+                if (kSfaByCtl && i < 2) sfa_by_ctl(i);
                 mbar_wait(bar(B_FULL + slot), (i / kSlots) & 1, abort_flag, p.err);
                 mbar_wait(bar(B_SFA_FULL + fb), (i >> 1) & 1, abort_flag, p.err);
                 if (i > 0) mbar_wait(bar(B_S_FREE), (i - 1) & 1, abort_flag, p.err);
@@ -938,8 +943,12 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
                                                                          (32 * q4 + lane) * 32 + 4 * kk);
             tmem_st32(tmem + kTSFB + 32 * hh + lane_base, rr);
             tmem_wait_st();
+            // every softmax warp writes a part (pass hh, its sub-partition): the MMA waits for all
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_SFB));
         }
-        if (hh == 0 && n_tiles > 0) {
+        if (!kSfaByCtl && hh == 0 && n_tiles > 0) {
             mbar_wait(bar(B_FULL + 0), 0, abort_flag, p.err);
             scales_to_tmem(smem + SM_STAGE + kCodeBytes, tmem + kTSFA + lane_base, lane);
             tc_fence_before();
@@ -998,24 +1007,32 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             // Probabilities against the running row maxima, computed speculatively in place:
             // p = 2^(s qs - m).  They stand unless some visible score exceeds its row's max by
             // more than 2^8 (a vote over the CTA); then the maxima move and p is recomputed.
+            // Sparse tile 0: the maxima are -inf, so the update below always runs; it skips this
+            // pass and the vote and works on the raw scores still in sv (a tile with no visible
+            // score leaves the maxima at -inf and every probability at 0).  In a sparse split
+            // of two tiles that is half the softmax work; dense keeps one code path (its
+            // registers are at the limit).
+            const bool first = kSparse && i == 0;
             bool grow = false;
+            if (!first) {
 #pragma unroll
-            for (int n4 = 0; n4 < 8; ++n4) {
-                const float4 q4 = reinterpret_cast<const float4*>(qs_h)[n4];
-                const float4 m4 = reinterpret_cast<const float4*>(M_h)[n4];
-                const int4 l4 = reinterpret_cast<const int4*>(lim_h)[n4];
-                const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
-                const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
-                const int lv[4] = {l4.x, l4.y, l4.z, l4.w};
+                for (int n4 = 0; n4 < 8; ++n4) {
+                    const float4 q4 = reinterpret_cast<const float4*>(qs_h)[n4];
+                    const float4 m4 = reinterpret_cast<const float4*>(M_h)[n4];
+                    const int4 l4 = reinterpret_cast<const int4*>(lim_h)[n4];
+                    const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+                    const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
+                    const int lv[4] = {l4.x, l4.y, l4.z, l4.w};
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const bool vis = tok_ok && (!per_row_lim || pos < lv[k]);
-                    const float x = fmaf(sv[4 * n4 + k], qv[k], -mv[k]);
-                    grow |= vis && x > kRescaleLog2;
-                    sv[4 * n4 + k] = vis ? ex2_approx(x) : 0.0f;
+                    for (int k = 0; k < 4; ++k) {
+                        const bool vis = tok_ok && (!per_row_lim || pos < lv[k]);
+                        const float x = fmaf(sv[4 * n4 + k], qv[k], -mv[k]);
+                        grow |= vis && x > kRescaleLog2;
+                        sv[4 * n4 + k] = vis ? ex2_approx(x) : 0.0f;
+                    }
                 }
             }
-            const bool any = named_bar_red_or(1, kSoftmaxThreads, grow);
+            const bool any = first || named_bar_red_or(1, kSoftmaxThreads, grow);
             uint32_t pk[16];
             if (!any) {
                 // common case: P is ready before PV(i-1) completes
@@ -1025,7 +1042,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
                 for (int k = 0; k < 16; ++k) pk[k] = pack_half2(sv[2 * k], sv[2 * k + 1]);
             } else {
                 // new row max = max(old, tile max); alpha = 2^(old - new)
-                load_scores();
+                if (!first) load_scores();
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {   // 16 rows at a time keeps the register count down
                     float xv[16];
