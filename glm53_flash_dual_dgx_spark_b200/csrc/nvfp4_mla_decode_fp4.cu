@@ -593,10 +593,11 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
     constexpr int SM_QS = C::SM_QS, SM_LIM = C::SM_LIM, SM_LSUM = C::SM_LSUM, SM_RED = C::SM_RED;
     constexpr int SM_ROWOFF = C::SM_ROWOFF, SM_FLAGS = C::SM_FLAGS, SM_TMASK = C::SM_TMASK, SM_BARS = C::SM_BARS;
     constexpr int SM_IDX = C::SM_IDX;
-    // Sparse: the control warpgroup writes tiles 0 and 1's pool scales into TMEM (their slots'
-    // first use), each warp its sub-partition's copy (warps 12-15 are sub-partitions 0-3), as
-    // the tiles land; on the softmax side tile 0's waited for the Q image and tile 1's sat
-    // between P(0) and QK(1).  Every later pool-scale write is the softmax warps'.
+    // Sparse: the control warpgroup writes tile 1's pool scales into TMEM (the slot's first
+    // use), each warp its sub-partition's copy (warps 12-15 are sub-partitions 0-3), as the
+    // tile lands; on the softmax side that write sat between P(0) and QK(1).  Tile 0's (set-up)
+    // and every later pool-scale write is the softmax warps'; the MMA warp writing tile 0's
+    // copy delayed QK(0) by 0.6 us.
     constexpr bool kSfaByCtl = kSparse;
     constexpr int B_FULL = C::B_FULL, B_FREE = C::B_FREE, B_QKD = C::B_QKD, B_SFA_FULL = C::B_SFA_FULL;
     constexpr int B_S_FULL = C::B_S_FULL, B_S_FREE = C::B_S_FREE, B_P_FULL = C::B_P_FULL, B_PV_DONE = C::B_PV_DONE;
@@ -676,7 +677,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = static_cast<uint32_t>(flags[0]);
-    auto sfa_by_ctl = [&](int j) {   // tile j < 2: ring slot j, TMEM scale slot j
+    auto sfa_by_ctl = [&](int j) {   // tile j < 2 (first ring pass): ring slot j, TMEM scale slot j
         mbar_wait(bar(B_FULL + j), 0, abort_flag, p.err);
         scales_to_tmem_narrow(smem + SM_STAGE + j * kSlotBytes + kCodeBytes,
                               tmem + kTSFA + 32 * j + (static_cast<uint32_t>(32 * (warp & 3)) << 16), lane);
@@ -697,9 +698,8 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
         for (int j = 0; j < kSlots && j < n_tiles; ++j)
             load_rows_gather4_x4(p, &tm_codes, &tm_scales, sbase + SM_STAGE + j * kSlotBytes, bar(B_FULL + j),
                                  tmask + 4 * j, sidx, idx_base, b, start + j * kTile, end, warp - kMmaWarp, lane);
-        // the MMA warp writes its copies in its loop, just before it waits for them
-        if (kSfaByCtl && warp != kMmaWarp)
-            for (int j = 0; j < 2 && j < n_tiles; ++j) sfa_by_ctl(j);
+        // the MMA warp writes its copy after QK(0) is issued
+        if (kSfaByCtl && warp != kMmaWarp && n_tiles > 1) sfa_by_ctl(1);
     }
     if (warp == kTmaWarp) {
         // ============================================================ TMA / bulk loads
@@ -793,7 +793,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
         for (int i = 0; i <= n_tiles; ++i) {
             if (i < n_tiles) {
                 const int slot = i % kSlots, fb = i & 1;
-                if (kSfaByCtl && i < 2) sfa_by_ctl(i);
+                if (kSfaByCtl && i == 1) sfa_by_ctl(1);
                 mbar_wait(bar(B_FULL + slot), (i / kSlots) & 1, abort_flag, p.err);
                 mbar_wait(bar(B_SFA_FULL + fb), (i >> 1) & 1, abort_flag, p.err);
                 if (i > 0) mbar_wait(bar(B_S_FREE), (i - 1) & 1, abort_flag, p.err);
@@ -948,7 +948,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(B_SFB));
         }
-        if (!kSfaByCtl && hh == 0 && n_tiles > 0) {
+        if (hh == 0 && n_tiles > 0) {
             mbar_wait(bar(B_FULL + 0), 0, abort_flag, p.err);
             scales_to_tmem(smem + SM_STAGE + kCodeBytes, tmem + kTSFA + lane_base, lane);
             tc_fence_before();
