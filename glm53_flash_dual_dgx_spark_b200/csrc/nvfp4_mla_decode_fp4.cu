@@ -56,6 +56,7 @@ constexpr int kProducerWarps = 4;
 constexpr int kMmaWarp = 12;                      // warpgroup 3: MMA issue,
 constexpr int kTmaWarp = 13;                      //   every TMA / bulk load, and two spare warps
 constexpr int kLoadBar = 2;                       // named barrier of the control warpgroup's shared loads
+constexpr int kRefillBar = 3;                     // named barrier of the sparse refill warps (13-15)
 constexpr int kThreads = 16 * 32;                 // 512
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
 constexpr uint32_t kRegsSoftmax = 168, kRegsProducer = 96, kRegsCtl = 80;
@@ -172,9 +173,12 @@ __device__ __forceinline__ void q_prep_row(const QPrepParams& p, int unit, int n
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
-    int e = (amax > 0.0f && amax <= 3.0e38f) ? ilogbf(amax) - 10 : 0;
+    // e = floor(log2 amax) - 10 from the exponent bits (a subnormal or zero row keeps e = 0 and
+    // its terms quantise to zero, as the reference data never has such rows in practice)
+    const int eb = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu);
+    int e = (eb > 0 && eb < 255) ? eb - 127 - 10 : 0;
     e = max(-100, min(100, e));
-    const float mul = ldexpf(1.0f, -e);
+    const float mul = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);   // 2^-e, exact
 #pragma unroll
     for (int j = 0; j < 16; ++j) x[j] *= mul;
     if (p.rope_q)   // rope dims 512 + 2 lane, +1, on the same power-of-two scale as the terms
@@ -184,12 +188,18 @@ __device__ __forceinline__ void q_prep_row(const QPrepParams& p, int unit, int n
     const int chunk = (lane & 15) >> 1;
 #pragma unroll
     for (int tt = 0; tt < 4; ++tt) {
-        float am = 0.0f;
+        // block amax as a tree (the chain of each term is the kernel's latency); the scale and
+        // its reciprocal need not be exact: they only place the codes, which the next terms
+        // correct, and the decode uses the stored e4m3 scale itself
+        float a8[8];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) am = fmaxf(am, fabsf(x[j]));
-        const uint8_t sb = am > 0.0f ? f32_to_e4m3(am / 6.0f) : static_cast<uint8_t>(0);
+        for (int j = 0; j < 8; ++j) a8[j] = fmaxf(fabsf(x[2 * j]), fabsf(x[2 * j + 1]));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) a8[j] = fmaxf(a8[j], a8[j + 4]);
+        const float am = fmaxf(fmaxf(a8[0], a8[2]), fmaxf(a8[1], a8[3]));
+        const uint8_t sb = am > 0.0f ? f32_to_e4m3(am * (1.0f / 6.0f)) : static_cast<uint8_t>(0);
         const float sf = e4m3_to_f32(sb);
-        const float inv = sf > 0.0f ? 1.0f / sf : 0.0f;
+        const float inv = sf > 0.0f ? rcp_approx(sf) : 0.0f;
         uint32_t wlo = 0, whi = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -376,51 +386,55 @@ __device__ __forceinline__ int64_t token_row(const Fp4Params& p, const int* sidx
 }
 
 // Sparse: the rows of tile `tile_start` into the ring slot at `slot_base` by TMA row gathers
-// (tile::gather4: four arbitrary pool rows per instruction, the box one row high): lane l
-// fetches rows 4l .. 4l + 3 of the tile as three gathers, the two 128-byte halves of their
-// codes (written 128-byte swizzled, the layout the dense path's tile boxes produce) and their
-// 32 scale bytes.  The TMA unit keeps the whole tile in flight, where per-thread 16-byte
-// copies were bound by the SM's issue and request rate.  A masked row (-1 padding, an
-// out-of-range entry, a position past `end`) is fetched from pool row 0: its bit stays clear
-// in the slot's valid-row mask, the softmax gives it probability 0 and the producers write
-// its V as zeros, so nothing of that row reaches the output.  Lane 0 writes the mask and arms
-// the barrier with the tile's bytes before any gather is issued.
-__device__ __forceinline__ void load_rows_gather4(const Fp4Params& p, const void* tm_codes, const void* tm_scales,
-                                                  uint32_t slot_base, uint32_t bar_full, uint32_t* slot_mask,
-                                                  const int* sidx, int idx_base, int b, int tile_start, int end,
-                                                  int lane) {
+// (tile::gather4: four arbitrary pool rows per instruction, the box one row high), issued by a
+// group of NW warps of the control warpgroup together: the issue of a gather4 serialises over
+// the lanes of a warp (measured, 148 CTAs x 16 tiles of 128 random rows: 3.6 us per tile from
+// one warp, 2.4 us from two, 1.9 us from four), so warp wq of the group takes mask words
+// wq, wq + NW, ... (word k: rows 32k .. 32k + 31), eight lanes of four rows per word.  Four
+// rows are three gathers: the two 128-byte halves of their codes (written 128-byte swizzled,
+// the layout the dense path's tile boxes produce) and their 32 scale bytes.  A masked row (-1
+// padding, an out-of-range entry, a position past `end`) is fetched from pool row 0: its bit
+// stays clear in the slot's valid-row mask, the softmax gives it probability 0 and the
+// producers write its V as zeros, so nothing of that row reaches the output.  Named barrier
+// `bar_id` (the group's NW x 32 threads) orders every mask word before the arming arrive
+// (warp 0 of the group) and that before any copy of the phase.
+template <int NW>
+__device__ __forceinline__ void load_rows_gather4_grp(const Fp4Params& p, const void* tm_codes, const void* tm_scales,
+                                                      uint32_t slot_base, uint32_t bar_full, uint32_t* slot_mask,
+                                                      const int* sidx, int idx_base, int b, int tile_start, int end,
+                                                      int wq, int lane, int bar_id) {
+    const int k = lane >> 3;                 // which of this warp's words
+    const int w = wq + NW * k;               // the mask word, rows 32w .. 32w + 31
+    const bool act = w < 4;
+    const int r0 = 32 * w + 4 * (lane & 7);
     int rows[4];
     uint32_t live = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const int pos = tile_start + 4 * lane + j;
-        const int64_t row = pos < end ? token_row<true>(p, sidx, true, idx_base, b, pos, true) : -1;
+        const int pos = tile_start + r0 + j;
+        const int64_t row = act && pos < end ? token_row<true>(p, sidx, true, idx_base, b, pos, true) : -1;
         live |= static_cast<uint32_t>(row >= 0) << j;
         rows[j] = row >= 0 ? static_cast<int>(row) : 0;
     }
-    // lane l holds rows 4l .. 4l+3.  bits[j] bit l: row 4l + j is live.  Mask word k covers rows
-    // 32k .. 32k+31, i.e. lanes 8k .. 8k+7: row 32k + 4m + j is bit 4m + j of word k.
     uint32_t bits[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) bits[j] = __ballot_sync(0xFFFFFFFFu, (live >> j) & 1u);
-    if (lane == 0) {   // the thread that arms the barrier writes the whole mask
+    if (act && (lane & 7) == 0) {   // row 32w + 4m + j is bit 4m + j of word w
+        uint32_t word = 0;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            uint32_t w = 0;
+        for (int j = 0; j < 4; ++j)
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-                for (int m = 0; m < 8; ++m) w |= ((bits[j] >> (8 * k + m)) & 1u) << (4 * m + j);
-            slot_mask[k] = w;
-        }
+            for (int m = 0; m < 8; ++m) word |= ((bits[j] >> (8 * k + m)) & 1u) << (4 * m + j);
+        slot_mask[w] = word;
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive_expect_tx(bar_full, kSlotBytes);
-    __syncwarp();
-    const int r0 = 4 * lane;
-    tma_gather4(slot_base + r0 * 128, tm_codes, 0, rows, bar_full);
-    tma_gather4(slot_base + 16384 + r0 * 128, tm_codes, 128, rows, bar_full);
-    tma_gather4(slot_base + kCodeBytes + r0 * 32, tm_scales, 256, rows, bar_full);
+    named_bar_sync(bar_id, NW * 32);   // every mask word written before the arming arrive
+    if (wq == 0 && lane == 0) mbar_arrive_expect_tx(bar_full, kSlotBytes);
+    named_bar_sync(bar_id, NW * 32);   // armed before any copy of the phase issues
+    if (act) {
+        tma_gather4(slot_base + r0 * 128, tm_codes, 0, rows, bar_full);
+        tma_gather4(slot_base + 16384 + r0 * 128, tm_codes, 128, rows, bar_full);
+        tma_gather4(slot_base + kCodeBytes + r0 * 32, tm_scales, 256, rows, bar_full);
+    }
 }
 
 // The prepared Q image of (sequence b, query group g) -> shared memory: Q-term codes, their
@@ -435,46 +449,6 @@ __device__ __forceinline__ void load_q_image(const Fp4Params& p, uint32_t sbase,
     bulk_copy_g2s(sbase + kQB, img, 2 * kCodeBytes, bar_q);
     bulk_copy_g2s(sbase + kPT, img + 2 * kCodeBytes, 2 * 4096, bar_q);
     bulk_copy_g2s(sbase + kQS, img + 2 * kCodeBytes + 2 * 4096, 256, bar_q);
-}
-
-// The same copy issued by the four warps of the control warpgroup together (the first ring
-// tiles, before the MMA warp has anything to issue): the issue of a gather4 serialises over
-// the lanes of a warp (measured: 128 rows take 3.6 us from one warp, 1.9 us from four), so
-// warp wq takes rows 32 wq .. 32 wq + 31, eight lanes of four rows, and writes mask word wq.
-// Warp 1 of the four arms the barrier once every word is written and before any copy issues.
-__device__ __forceinline__ void load_rows_gather4_x4(const Fp4Params& p, const void* tm_codes, const void* tm_scales,
-                                                     uint32_t slot_base, uint32_t bar_full, uint32_t* slot_mask,
-                                                     const int* sidx, int idx_base, int b, int tile_start, int end,
-                                                     int wq, int lane) {
-    int rows[4];
-    uint32_t live = 0;
-    const int r0 = 32 * wq + 4 * lane;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int pos = tile_start + r0 + j;
-        const int64_t row = lane < 8 && pos < end ? token_row<true>(p, sidx, true, idx_base, b, pos, true) : -1;
-        live |= static_cast<uint32_t>(row >= 0) << j;
-        rows[j] = row >= 0 ? static_cast<int>(row) : 0;
-    }
-    uint32_t bits[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) bits[j] = __ballot_sync(0xFFFFFFFFu, (live >> j) & 1u);
-    if (lane == 0) {   // row 32 wq + 4m + j is bit 4m + j of word wq
-        uint32_t w = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-            for (int m = 0; m < 8; ++m) w |= ((bits[j] >> m) & 1u) << (4 * m + j);
-        slot_mask[wq] = w;
-    }
-    named_bar_sync(kLoadBar, 128);   // every mask word written before the arming arrive
-    if (wq == 1 && lane == 0) mbar_arrive_expect_tx(bar_full, kSlotBytes);
-    named_bar_sync(kLoadBar, 128);   // armed before any copy of the phase issues
-    if (lane < 8) {
-        tma_gather4(slot_base + r0 * 128, tm_codes, 0, rows, bar_full);
-        tma_gather4(slot_base + 16384 + r0 * 128, tm_codes, 128, rows, bar_full);
-        tma_gather4(slot_base + kCodeBytes + r0 * 32, tm_scales, 256, rows, bar_full);
-    }
 }
 
 // Pool scales of the tile in `slot` -> TMEM scale-factor columns `col` of this warp's
@@ -696,10 +670,59 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             tma_prefetch_desc(&tm_scales);
         }
         for (int j = 0; j < kSlots && j < n_tiles; ++j)
-            load_rows_gather4_x4(p, &tm_codes, &tm_scales, sbase + SM_STAGE + j * kSlotBytes, bar(B_FULL + j),
-                                 tmask + 4 * j, sidx, idx_base, b, start + j * kTile, end, warp - kMmaWarp, lane);
+            load_rows_gather4_grp<4>(p, &tm_codes, &tm_scales, sbase + SM_STAGE + j * kSlotBytes, bar(B_FULL + j),
+                                     tmask + 4 * j, sidx, idx_base, b, start + j * kTile, end, warp - kMmaWarp,
+                                     lane, kLoadBar);
         // the MMA warp writes its copy after QK(0) is issued
         if (kSfaByCtl && warp != kMmaWarp && n_tiles > 1) sfa_by_ctl(1);
+        if (warp != kMmaWarp) {
+            // ======================================================== sparse refills
+            // tile j -> slot j % kSlots once QK(j - kSlots) and the producers are done with it,
+            // gathered by the load warp and the two spare warps together
+            const int wq = warp - kTmaWarp;
+            int issued = n_tiles < kSlots ? n_tiles : kSlots;   // tile j completes phase j / kSlots of its slot
+            // Splits longer than the index window: after tile t is issued, the load warp loads
+            // the rows of tile t + kSlots into registers (window slot (t + kSlots) % kIdxTiles,
+            // whose tile t + kSlots - kIdxTiles was issued long before) and stores them before
+            // the next issue, so no copy waits on a table load.
+            static_assert(2 * kSlots <= kIdxTiles, "index window covers the refill distance");
+            const bool refill = idx_count > kMaxIdx;
+            int pend[4] = {-1, -1, -1, -1};
+            int pend_tile = -1;
+#pragma unroll 1
+            for (int i = 0; i + kSlots < n_tiles; ++i) {
+                const int slot = i % kSlots;
+                const uint32_t sph = (i / kSlots) & 1;
+                const bool f = mbar_wait(bar(B_FREE + slot), sph, abort_flag, p.err);
+                const bool d = mbar_wait(bar(B_QKD + slot), sph, abort_flag, p.err);
+                // after an abort nothing more is issued (the drain below waits for what was);
+                // the three warps decide together, so none is left at a named barrier
+                if (named_bar_red_or(kRefillBar, 96, !(f && d) || *abort_flag)) break;
+                if (wq == 0 && pend_tile >= 0) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) sidx[(pend_tile % kIdxTiles) * kTile + 32 * k + lane] = pend[k];
+                }
+                fence_proxy_async_smem();
+                named_bar_sync(kRefillBar, 96);   // the refreshed row ids visible to the group
+                const int t = i + kSlots;
+                load_rows_gather4_grp<3>(p, &tm_codes, &tm_scales, sbase + SM_STAGE + slot * kSlotBytes,
+                                         bar(B_FULL + slot), tmask + 4 * slot, sidx, idx_base, b, start + t * kTile,
+                                         end, wq, lane, kRefillBar);
+                issued = t + 1;
+                pend_tile = -1;
+                if (wq == 0 && refill && t + kSlots >= kIdxTiles && t + kSlots < n_tiles) {
+                    pend_tile = t + kSlots;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int pos = start + pend_tile * kTile + 32 * k + lane;
+                        pend[k] = pos < end ? __ldg(p.tables + b * p.tables_stride + pos) : -1;
+                    }
+                }
+            }
+            if (wq == 0)
+                for (int j = issued > kSlots ? issued - kSlots : 0; j < issued; ++j)
+                    mbar_drain_wait(bar(B_FULL + j % kSlots), (j / kSlots) & 1);
+        }
     }
     if (warp == kTmaWarp) {
         // ============================================================ TMA / bulk loads
@@ -711,48 +734,7 @@ decode_fp4_kernel(const __grid_constant__ Fp4Params p, const __grid_constant__ C
             tma_prefetch_desc(&tm_scales);
         }
         if constexpr (kSparse) {
-            // tile j -> slot j % kSlots once QK(j - kSlots) and the producers are done with it;
-            // the first kSlots tiles were issued by the whole group above
-            int issued = n_tiles < kSlots ? n_tiles : kSlots;   // tile j completes phase j / kSlots of its slot
-            // Splits longer than the index window: after tile t is issued, the rows of tile
-            // t + kSlots are loaded into registers (window slot (t + kSlots) % kIdxTiles, whose
-            // tile t + kSlots - kIdxTiles was issued long before) and stored before the next
-            // issue, so no copy waits on a table load.
-            static_assert(2 * kSlots <= kIdxTiles, "index window covers the refill distance");
-            const bool refill = idx_count > kMaxIdx;
-            int pend[4] = {-1, -1, -1, -1};
-            int pend_tile = -1;
-#pragma unroll 1
-            for (int i = 0; i + kSlots < n_tiles; ++i) {
-                const int slot = i % kSlots;
-                const uint32_t sph = (i / kSlots) & 1;
-                const bool f = mbar_wait(bar(B_FREE + slot), sph, abort_flag, p.err);
-                const bool d = mbar_wait(bar(B_QKD + slot), sph, abort_flag, p.err);
-                // after an abort nothing more is issued (the drain below waits for what was)
-                if (!__all_sync(0xFFFFFFFFu, f && d && !*abort_flag)) break;
-                if (pend_tile >= 0) {
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) sidx[(pend_tile % kIdxTiles) * kTile + 32 * k + lane] = pend[k];
-                    __syncwarp();
-                }
-                fence_proxy_async_smem();
-                const int t = i + kSlots;
-                load_rows_gather4(p, &tm_codes, &tm_scales, sbase + SM_STAGE + slot * kSlotBytes,
-                                  bar(B_FULL + slot), tmask + 4 * slot, sidx, idx_base, b, start + t * kTile, end,
-                                  lane);
-                issued = t + 1;
-                pend_tile = -1;
-                if (refill && t + kSlots >= kIdxTiles && t + kSlots < n_tiles) {
-                    pend_tile = t + kSlots;
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const int pos = start + pend_tile * kTile + 32 * k + lane;
-                        pend[k] = pos < end ? __ldg(p.tables + b * p.tables_stride + pos) : -1;
-                    }
-                }
-            }
-            for (int j = issued > kSlots ? issued - kSlots : 0; j < issued; ++j)
-                mbar_drain_wait(bar(B_FULL + j % kSlots), (j / kSlots) & 1);
+            // the row gathers are issued above
         } else if (lane == 0) {
             load_q_image<SM_QB, SM_PT, SM_QS>(p, sbase, bar(B_Q), b, g);
             int issued = 0;   // tiles loaded; tile j completes phase j / kSlots of slot j % kSlots
