@@ -204,6 +204,30 @@ __device__ __forceinline__ void mbar_drain_wait(uint32_t bar, uint32_t parity) {
         if (globaltimer_ns() - t0 > NVFP4KV_WAIT_TIMEOUT_NS) return;
 }
 
+// ------------------------------------------------------------------ thread-block clusters
+// Every thread of every CTA of the cluster arrives (release) and waits (acquire): a cluster-wide
+// barrier that also orders shared-memory accesses across the cluster's CTAs.  Like
+// __syncthreads it needs every thread to reach it; the kernels that use it have no early exit.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The address in CTA `rank`'s shared memory of this CTA's shared address `addr`.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ int ld_cluster_s32(uint32_t addr) {
+    int v;
+    asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

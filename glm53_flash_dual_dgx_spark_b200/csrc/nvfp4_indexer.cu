@@ -17,9 +17,11 @@
 //                       to bf16 in shared memory (code x e4m3 scale has at most 5
 //                       significant bits), K . Q^T on the tensor cores (wmma bf16, fp32
 //                       accumulation), then the ReLU-weighted head sum per position.
-//   index_topk_kernel   one block per query: an 8-pass 4-bit radix select of the k-th largest
-//                       score, then the selected positions written in ascending order (ties
-//                       at the threshold go to the lowest positions), mapped to pool rows.
+//   index_topk_kernel   one thread-block cluster of 8 CTAs per query, each CTA an eighth of
+//                       the positions: an 8-pass 4-bit radix select of the k-th largest score
+//                       (digit counts exchanged through distributed shared memory), then the
+//                       selected positions written in ascending order (ties at the threshold
+//                       go to the lowest positions), mapped to pool rows.
 #include <mma.h>
 
 #include "abi_common.h"
@@ -183,7 +185,7 @@ __global__ void __launch_bounds__(256) index_score_kernel(const ScoreParams p, i
 }
 
 // ------------------------------------------------------------------ top-k selection
-constexpr int kKThreads = 1024;
+constexpr int kKThreads = 512;
 
 // Order-preserving map of an fp32 score to an unsigned key (larger score -> larger key).
 __device__ __forceinline__ uint32_t score_key(float f) {
@@ -201,41 +203,76 @@ struct TopkParams {
     int page_shift, max_seq_len, topk;
     int32_t* out_rows;            // [batch][topk]: pool rows of the selected positions, ascending; -1 after
     int32_t* out_count;           // [batch]: min(seq_len, topk)
+    int staged;                   // every CTA's chunk fits kStageMax keys: staged in shared memory
 };
 
+// One query per cluster of kCl CTAs, CTA r taking positions [r c, (r + 1) c) of the query's
+// n scores (c = ceil(n / kCl), a multiple of kKThreads).  A radix select with 4-bit digits,
+// most significant first, finds the k-th largest key: each thread counts the 16 digits of its
+// candidates in registers (shared-memory atomics serialise on the few bins the scores crowd
+// into), a CTA's warps reduce them, and every CTA reads all kCl CTAs' counts of the pass
+// through distributed shared memory after one cluster barrier (the counts are double-buffered
+// by pass, so a CTA overwrites a buffer only two passes after it was written, when every peer
+// has read it) and picks the same digit.  Then every position above the threshold and the
+// first need_eq ties, in ascending position order, go out: a CTA's output offset is the count
+// taken by the CTAs before it (from their (above, tie) counts, after one more cluster barrier),
+// and within a CTA coalesced rounds of kKThreads positions place them by ballot prefix counts.
+// A last cluster barrier keeps every CTA alive until its peers' remote reads are done.  A
+// CTA's keys are staged once in shared memory when its chunk fits (kStageMax keys: 128K-token
+// contexts and somewhat beyond), so the eight passes and the selection read them there; a
+// longer chunk is read from the score buffer on every pass.
+constexpr int kCl = 8;
+constexpr int kStageMax = 40960;                    // keys a CTA stages (160 KB)
+
 __global__ void __launch_bounds__(kKThreads) index_topk_kernel(const TopkParams p, int32_t* err) {
-    __shared__ int hist[32][17];                    // per-warp counts of the 16 digits
-    __shared__ uint32_t s_prefix, s_mask;
-    __shared__ int s_remaining;
-    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int n = clamp_len(p.seq_lens, b, p.max_seq_len, err);
+    extern __shared__ __align__(16) uint32_t skeys[];  // [chunk] when staged
+    __shared__ int hist[kKThreads / 32][17];        // per-warp counts of the 16 digits
+    __shared__ int cta_cnt[2][16];                  // this CTA's digit counts, by pass parity
+    __shared__ int s_part[kCl][16];                 // the peers' counts of the pass
+    __shared__ int s_tot[16];                       // the cluster's counts of the pass
+    __shared__ int sel[2];                          // this CTA's (above, tie) counts
+    __shared__ int s_before[2];                     // the same, summed over the CTAs before it
+    constexpr int kWarps = kKThreads / 32;
+    const int rank = static_cast<int>(cluster_rank());
+    const int b = blockIdx.x / kCl, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n = clamp_len(p.seq_lens, b, p.max_seq_len, rank == 0 ? err : nullptr);
     const int k = n < p.topk ? n : p.topk;
+    const int chunk = ((n + kCl - 1) / kCl + kKThreads - 1) / kKThreads * kKThreads;
+    const int lo = min(n, rank * chunk), hi = min(n, lo + chunk);
     const float* sc = p.scores + static_cast<int64_t>(b) * p.ld;
     int32_t* out = p.out_rows + static_cast<int64_t>(b) * p.topk;
-    if (tid == 0) p.out_count[b] = k;
-    uint32_t thr = 0;
-    int need_eq = 0;                                // positions with key == thr to take
-    if (k < n) {
-        if (tid == 0) {
-            s_prefix = 0u;
-            s_mask = 0u;
-            s_remaining = k;
-        }
+    if (tid == 0 && rank == 0) p.out_count[b] = k;
+    const bool all = k >= n;                        // the same in every CTA of the cluster
+    const bool staged = p.staged != 0;              // chunk <= kStageMax for every query of the call
+    if (staged) {
+        for (int pos = lo + tid; pos < hi; pos += kKThreads) skeys[pos - lo] = score_key(sc[pos]);
         __syncthreads();
-        // 4-bit digits, most significant first: each thread counts the 16 digits of its
-        // candidates in registers (no shared-memory atomics: the scores crowd into a few bins,
-        // where atomics serialise), the warps reduce them, and warp 0 finds the digit at which
-        // the count from the top reaches the number still wanted
-        for (int shift = 28; shift >= 0; shift -= 4) {
-            const uint32_t prefix = s_prefix, mask = s_mask;
+    }
+    auto key = [&](int pos) -> uint32_t { return staged ? skeys[pos - lo] : score_key(sc[pos]); };
+    uint32_t prefix = 0u, mask = 0u;
+    int remaining = k;
+    if (!all) {
+        for (int pass = 0; pass < 8; ++pass) {
+            const int shift = 28 - 4 * pass;
+            // the 16 counts as 8-bit fields of two 64-bit registers, drained into integers
+            // every 255 keys a thread sees (once per pass for a staged chunk: <= 80 keys)
             int c[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) c[j] = 0;
-            for (int pos = tid; pos < n; pos += kKThreads) {
-                const uint32_t u = score_key(sc[pos]);
-                const uint32_t d = (u & mask) == prefix ? (u >> shift) & 15u : 16u;
+            for (int base = lo + tid; base < hi; base += 255 * kKThreads) {
+                uint64_t c_lo = 0, c_hi = 0;
+                const int lim = min(hi, base + 255 * kKThreads);
+                for (int pos = base; pos < lim; pos += kKThreads) {
+                    const uint32_t u = key(pos);
+                    if ((u & mask) == prefix) {
+                        const uint32_t d = (u >> shift) & 15u;
+                        const uint64_t one = 1ull << (8 * (d & 7u));
+                        if (d < 8) c_lo += one;
+                        else c_hi += one;
+                    }
+                }
 #pragma unroll
-                for (int j = 0; j < 16; ++j) c[j] += d == static_cast<uint32_t>(j);
+                for (int j = 0; j < 16; ++j) c[j] += static_cast<int>(((j < 8 ? c_lo : c_hi) >> (8 * (j & 7))) & 0xFFu);
             }
 #pragma unroll
             for (int j = 0; j < 16; ++j) c[j] = __reduce_add_sync(0xFFFFFFFFu, c[j]);
@@ -243,76 +280,102 @@ __global__ void __launch_bounds__(kKThreads) index_topk_kernel(const TopkParams 
 #pragma unroll
                 for (int j = 0; j < 16; ++j) hist[warp][j] = c[j];
             __syncthreads();
-            if (warp == 0) {
-                const int remaining = s_remaining;
-                const int digit = 15 - lane;                 // lane 0: the highest digit
-                int cnt = 0;
-                if (lane < 16)
-                    for (int w = 0; w < 32; ++w) cnt += hist[w][digit];
-                int incl = cnt;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-                    if (lane >= o) incl += y;
-                }
-                const unsigned hit = __ballot_sync(0xFFFFFFFFu, lane < 16 && incl >= remaining);
-                const int first = __ffs(hit) - 1;            // there always is one
-                const int above = __shfl_sync(0xFFFFFFFFu, incl - cnt, first);
-                if (lane == 0) {
-                    s_prefix |= static_cast<uint32_t>(15 - first) << shift;
-                    s_mask |= 15u << shift;
-                    s_remaining = remaining - above;
-                }
+            if (tid < 16) {
+                int t = 0;
+                for (int w = 0; w < kWarps; ++w) t += hist[w][tid];
+                cta_cnt[pass & 1][tid] = t;
+            }
+            cluster_sync();                         // every CTA's counts of this pass are out
+            if (tid < 16 * kCl) {                   // one remote load per thread, all in flight
+                const int r = tid >> 4, j = tid & 15;
+                s_part[r][j] = ld_cluster_s32(cluster_map(smem_u32(&cta_cnt[pass & 1][j]), static_cast<uint32_t>(r)));
             }
             __syncthreads();
+            if (tid < 16) {
+                int t = 0;
+#pragma unroll
+                for (int r = 0; r < kCl; ++r) t += s_part[r][tid];
+                s_tot[tid] = t;
+            }
+            __syncthreads();
+            // the digit at which the count from the top reaches the number still wanted (every
+            // thread computes it from the same totals)
+            int above = 0, digit = 0;
+            for (int dg = 15; dg >= 0; --dg) {
+                const int t = s_tot[dg];
+                if (above + t >= remaining) {
+                    digit = dg;
+                    break;
+                }
+                above += t;
+            }
+            prefix |= static_cast<uint32_t>(digit) << shift;
+            mask |= 15u << shift;
+            remaining -= above;
         }
-        thr = s_prefix;
-        need_eq = s_remaining;
     }
-    // selection in ascending position order, in coalesced rounds of 1024 positions: the rank of
-    // an equal-to-threshold position among the ties, and its output slot, are block prefix
-    // counts (warp ballots, then the warps' totals) carried from round to round
-    __shared__ int cnt[32];
-    int eq_before = 0, out_before = 0;
-    for (int base = 0; base < n; base += kKThreads) {
-        const int pos = base + tid;
-        const uint32_t u = pos < n ? score_key(sc[pos]) : 0u;
-        const bool all = k >= n;
-        const bool gt = pos < n && !all && u > thr;
-        const bool eq = pos < n && !all && u == thr;
-        const unsigned below = (1u << lane) - 1u;
-        // rank of this tie among the round's ties before it
+    const uint32_t thr = prefix;
+    const int need_eq = all ? 0 : remaining;        // ties (key == thr) to take, lowest positions first
+    // Selection: warp w walks the contiguous positions [lo + w wc, lo + (w + 1) wc) of this
+    // CTA's chunk (wc = chunk / kWarps, a multiple of 32) in rounds of 32: a first walk counts
+    // the positions above the threshold and the ties, whose sums over the warps and then over
+    // the CTAs before this one (after a cluster barrier) give each warp its offsets, and a
+    // second walk writes them in ascending order (ballot prefix counts within a round).
+    const int wc = chunk / kWarps;
+    const int wlo = min(hi, lo + warp * wc), whi = min(hi, wlo + wc);
+    const unsigned below = (1u << lane) - 1u;
+    int w_gt = 0, w_eq = 0;
+    if (!all)
+        for (int base = wlo; base < whi; base += 32) {
+            const int pos = base + lane;
+            const uint32_t u = pos < whi ? key(pos) : 0u;
+            w_gt += __popc(__ballot_sync(0xFFFFFFFFu, pos < whi && u > thr));
+            w_eq += __popc(__ballot_sync(0xFFFFFFFFu, pos < whi && u == thr));
+        }
+    if (lane == 0) {
+        hist[warp][2] = w_gt;
+        hist[warp][3] = w_eq;
+    }
+    __syncthreads();
+    if (tid < 2) {
+        int t = 0;
+        for (int w = 0; w < kWarps; ++w) t += hist[w][2 + tid];
+        sel[tid] = t;
+    }
+    cluster_sync();                                 // every CTA's (above, tie) counts are out
+    if (tid < 2) {
+        const uint32_t a = smem_u32(&sel[tid]);
+        int t = 0;
+        for (int r = 0; r < rank; ++r) t += ld_cluster_s32(cluster_map(a, static_cast<uint32_t>(r)));
+        s_before[tid] = t;
+    }
+    __syncthreads();
+    int gt_off = 0, eq_off = 0;
+    for (int w = 0; w < warp; ++w) {
+        gt_off += hist[w][2];
+        eq_off += hist[w][3];
+    }
+    int eq_before = s_before[1] + eq_off;                       // ties before this warp's range
+    int out_before = all ? wlo : s_before[0] + gt_off + min(eq_before, need_eq);
+    for (int base = wlo; base < whi; base += 32) {
+        const int pos = base + lane;
+        const bool in = pos < whi;
+        const uint32_t u = in ? key(pos) : 0u;
+        const bool eq = in && !all && u == thr;
         const unsigned beq = __ballot_sync(0xFFFFFFFFu, eq);
-        if (lane == 0) cnt[warp] = __popc(beq);
-        __syncthreads();
-        int eq_off = 0, eq_round = 0;
-        for (int w = 0; w < 32; ++w) {
-            const int c = cnt[w];
-            eq_off += w < warp ? c : 0;
-            eq_round += c;
-        }
-        __syncthreads();
-        const int rank = eq_before + eq_off + __popc(beq & below);
-        const bool take = (all && pos < n) || gt || (eq && rank < need_eq);
+        const bool take = (all && in) || (in && !all && u > thr) || (eq && eq_before + __popc(beq & below) < need_eq);
         const unsigned btk = __ballot_sync(0xFFFFFFFFu, take);
-        if (lane == 0) cnt[warp] = __popc(btk);
-        __syncthreads();
-        int tk_off = 0, tk_round = 0;
-        for (int w = 0; w < 32; ++w) {
-            const int c = cnt[w];
-            tk_off += w < warp ? c : 0;
-            tk_round += c;
-        }
-        __syncthreads();
-        const int slot = out_before + tk_off + __popc(btk & below);
+        const int slot = out_before + __popc(btk & below);
         if (take && slot < p.topk) {   // exactly k are taken; the bound only guards the row
             const int64_t row = index_row(p.tables, p.tables_stride, b, pos, p.page_shift, p.num_pages);
             out[slot] = row >= 0 ? static_cast<int32_t>(row) : -1;
         }
-        eq_before += eq_round;
-        out_before += tk_round;
+        eq_before += __popc(beq);
+        out_before += __popc(btk);
     }
-    for (int j = k + tid; j < p.topk; j += kKThreads) out[j] = -1;
+    if (rank == kCl - 1)
+        for (int j = k + tid; j < p.topk; j += kKThreads) out[j] = -1;
+    cluster_sync();                                 // no CTA exits while a peer reads its counts
 }
 
 }  // namespace
@@ -385,6 +448,34 @@ extern "C" int nvfp4kv_index_topk(const void* q, int64_t q_stride_b, int64_t q_s
     tp.tables = tables; tp.tables_stride = tables_stride; tp.seq_lens = seq_lens;
     tp.num_pages = pool_rows / page_size; tp.page_shift = shift; tp.max_seq_len = max_seq_len; tp.topk = topk;
     tp.out_rows = out_rows; tp.out_count = out_count;
-    index_topk_kernel<<<static_cast<unsigned>(batch), kKThreads, 0, st>>>(tp, err_flag);
+    // chunk per CTA for the longest query: ceil(max_seq_len / kCl) rounded up to kKThreads
+    const int64_t chunk = ((static_cast<int64_t>(max_seq_len) + kCl - 1) / kCl + kKThreads - 1) / kKThreads * kKThreads;
+    tp.staged = chunk <= kStageMax ? 1 : 0;
+    const size_t stage_bytes = tp.staged ? static_cast<size_t>(chunk) * 4 : 0;
+    {
+        static int topk_attr_done[64] = {0};
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) return fail(NVFP4KV_ECUDA, "cudaGetDevice failed");
+        if (dev < 0 || dev >= 64 || !topk_attr_done[dev]) {
+            const cudaError_t e = cudaFuncSetAttribute(index_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       kStageMax * 4);
+            if (e != cudaSuccess) return fail(NVFP4KV_ECUDA, "index_topk: smem attribute: %s", cudaGetErrorString(e));
+            if (dev >= 0 && dev < 64) topk_attr_done[dev] = 1;
+        }
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(batch) * kCl);
+    cfg.blockDim = dim3(kKThreads);
+    cfg.dynamicSmemBytes = stage_bytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kCl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, index_topk_kernel, tp, err_flag);
+    if (le != cudaSuccess) return fail(NVFP4KV_ECUDA, "index_topk: selection launch: %s", cudaGetErrorString(le));
     return check_launch("nvfp4kv_index_topk (selection)");
 }
