@@ -14,9 +14,11 @@
 //
 // Kernels:
 //   index_score_kernel  one block per (query, run of 8 128-position tiles): keys dequantised exactly
-//                       to bf16 in shared memory (code x e4m3 scale has at most 5
-//                       significant bits), K . Q^T on the tensor cores (wmma bf16, fp32
-//                       accumulation), then the ReLU-weighted head sum per position.
+//                       to fp16 in shared memory by the hardware conversions (code x e4m3
+//                       scale has at most 5 significant bits), q in fp16 after an exact
+//                       power-of-two scale per head (folded into the head's weight), K . Q^T on
+//                       the tensor cores (wmma fp16, fp32 accumulation), then the ReLU-weighted
+//                       head sum per position.
 //   index_topk_kernel   one thread-block cluster of 8 CTAs per query, each CTA an eighth of
 //                       the positions: an 8-pass 4-bit radix select of the k-th largest score
 //                       (digit counts exchanged through distributed shared memory), then the
@@ -36,10 +38,13 @@ constexpr int kIDim = NVFP4KV_INDEX_DIM;            // 128
 constexpr int kIRow = NVFP4KV_INDEX_ROW_BYTES;      // 72
 // Shared-memory row strides padded by 16 bytes: rows 256 bytes apart would put every row of a
 // 16 x 16 fragment load in the same banks.
-constexpr int kQLd = kIDim + 8;                     // bf16 elements
+constexpr int kQLd = kIDim + 8;                     // fp16 elements
 constexpr int kKLd = kIDim + 8;
 constexpr int kSLd = kIHeads + 4;                   // fp32 elements
-constexpr int kScoreSmem = kIHeads * kQLd * 2 + kITile * kKLd * 2 + kITile * kSLd * 4;   // 87040
+// The fp32 head scores of a tile reuse the key tile's space once the products are done (the
+// same 34,816 bytes), so four blocks fit on an SM.
+static_assert(kITile * kSLd * 4 == kITile * kKLd * 2, "score staging aliases the key tile");
+constexpr int kScoreSmem = kIHeads * kQLd * 2 + kITile * kKLd * 2;   // 52224
 
 struct ScoreParams {
     const __nv_bfloat16* q;       // [batch][heads][128], row strides below
@@ -72,12 +77,6 @@ __device__ __forceinline__ int64_t index_row(const int32_t* tables, int64_t stri
     return (static_cast<int64_t>(pg) << shift) | (pos & ((1 << shift) - 1));
 }
 
-__device__ __forceinline__ float e2m1_val(uint32_t c) {
-    const uint32_t mag = c & 7u, e = mag >> 1, m = mag & 1u;
-    const float v = e == 0 ? 0.5f * m : __uint_as_float(((126u + e) << 23) | (m << 22));
-    return (c & 8u) ? -v : v;
-}
-
 // One thread's share of a key tile: position tid >> 1, half tid & 1 (64 elements = 4 blocks):
 // 32 code bytes and 4 scale bytes, loaded ahead of their use.
 struct KeyPart {
@@ -99,24 +98,25 @@ __device__ __forceinline__ KeyPart load_key_part(const ScoreParams& p, int b, in
     return k;
 }
 
-// Dequantise a key part into the bf16 tile row (code x scale is exact in bf16: at most 5
-// significant bits), zeros for a masked position.
+// Dequantise a key part into the fp16 tile row with the hardware conversions (e2m1 pair ->
+// f16x2, e4m3 pair -> f16x2, one f16x2 multiply): code x scale is exact in fp16 (at most 5
+// significant bits, magnitudes 2^-10 .. 2688), zeros for a masked position.
 __device__ __forceinline__ void store_key_part(const KeyPart& k, uint32_t* dst) {
     if (!k.ok) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) dst[j] = 0u;
         return;
     }
+    const uint32_t s01 = e4m3x2_to_f16x2(static_cast<uint16_t>(k.s & 0xFFFFu));
+    const uint32_t s23 = e4m3x2_to_f16x2(static_cast<uint16_t>(k.s >> 16));
+    const uint32_t sb[4] = {(s01 & 0xFFFFu) * 0x10001u, (s01 >> 16) * 0x10001u, (s23 & 0xFFFFu) * 0x10001u,
+                            (s23 >> 16) * 0x10001u};
 #pragma unroll
     for (int blk = 0; blk < 4; ++blk) {
-        const float s = e4m3_to_f32(static_cast<uint8_t>(k.s >> (8 * blk)));
         const uint32_t w2[2] = {k.c[blk].x, k.c[blk].y};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const uint32_t byte = (w2[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-            const __nv_bfloat162 v = __floats2bfloat162_rn(e2m1_val(byte & 15u) * s, e2m1_val(byte >> 4) * s);
-            dst[8 * blk + j] = *reinterpret_cast<const uint32_t*>(&v);
-        }
+        for (int j = 0; j < 8; ++j)
+            dst[8 * blk + j] = hmul2_u32(e2m1x2_to_f16x2((w2[j >> 2] >> (8 * (j & 3))) & 0xFFu), sb[blk]);
     }
 }
 
@@ -126,9 +126,9 @@ constexpr int kTilesPerBlock = 8;
 
 __global__ void __launch_bounds__(256) index_score_kernel(const ScoreParams p, int32_t* err) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem);              // [64 heads][kQLd]
-    __nv_bfloat16* ks = qs + kIHeads * kQLd;                                  // [128 positions][kKLd]
-    float* ss = reinterpret_cast<float*>(ks + kITile * kKLd);                 // [128 positions][kSLd]
+    __half* qs = reinterpret_cast<__half*>(smem);                            // [64 heads][kQLd] fp16
+    __half* ks = qs + kIHeads * kQLd;                                        // [128 positions][kKLd] fp16
+    float* ss = reinterpret_cast<float*>(ks);                                 // [128 positions][kSLd], after the products
     __shared__ float ws[kIHeads];
     const int runs = (p.tiles + kTilesPerBlock - 1) / kTilesPerBlock;
     const int b = blockIdx.x / runs, run = blockIdx.x % runs;
@@ -137,11 +137,40 @@ __global__ void __launch_bounds__(256) index_score_kernel(const ScoreParams p, i
     const int t1 = min(min(t0 + kTilesPerBlock, p.tiles), (L + kITile - 1) / kITile);
     if (t0 >= t1) return;                            // the whole block: nothing visible here
     const int tid = threadIdx.x, warp = tid >> 5;
-    for (int i = tid; i < kIHeads * kIDim / 8; i += blockDim.x) {
-        const int h = i >> 4, c = i & 15;
-        *reinterpret_cast<uint4*>(qs + h * kQLd + 8 * c) = ldg_nc_v4(p.q + b * p.q_sb + h * p.q_sh + 8 * c);
+    {
+        // q in fp16 for the fp16 tensor-core product: head h is scaled by 2^(10 - e_h), e_h =
+        // floor(log2 max|q_h|), which is exact and keeps the head inside fp16's range, and its
+        // weight by 2^(e_h - 10) (max(c x, 0) = c max(x, 0) for c > 0).  Four threads per head,
+        // 32 dims each.
+        const int h = tid >> 2, c0 = 32 * (tid & 3);
+        const __nv_bfloat16* src = p.q + b * p.q_sb + h * p.q_sh + c0;
+        uint4 v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = ldg_nc_v4(src + 8 * j);
+        float x[32];
+        float am = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t w4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                x[8 * j + 2 * t] = __uint_as_float(w4[t] << 16);
+                x[8 * j + 2 * t + 1] = __uint_as_float(w4[t] & 0xFFFF0000u);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) am = fmaxf(am, fabsf(x[j]));
+        am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, 1));
+        am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, 2));
+        const int eb = static_cast<int>((__float_as_uint(am) >> 23) & 0xFFu);   // biased exponent
+        const int e = (eb > 0 && eb < 255) ? eb - 127 : 0;
+        const int sh = max(-100, min(100, 10 - e));
+        const float mul = __uint_as_float(static_cast<uint32_t>(127 + sh) << 23);   // 2^sh
+        uint32_t* dst = reinterpret_cast<uint32_t*>(qs + h * kQLd + c0);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) dst[j] = pack_half2(x[2 * j] * mul, x[2 * j + 1] * mul);
+        if ((tid & 3) == 0) ws[h] = __ldg(p.w + b * p.w_sb + h) * __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
     }
-    if (tid < kIHeads) ws[tid] = __ldg(p.w + b * p.w_sb + tid);
     const int tok = tid >> 1, half = tid & 1;
     uint32_t* kdst = reinterpret_cast<uint32_t*>(ks + tok * kKLd + 64 * half);
     KeyPart next = load_key_part(p, b, t0 * kITile + tok, L, half);
@@ -159,15 +188,16 @@ __global__ void __launch_bounds__(256) index_score_kernel(const ScoreParams p, i
         for (int n = 0; n < 4; ++n) wmma::fill_fragment(acc[n], 0.0f);
 #pragma unroll
         for (int kk = 0; kk < kIDim / 16; ++kk) {
-            wmma::fragment<wmma::matrix_a, 16, 16, 16, __nv_bfloat16, wmma::row_major> a;
+            wmma::fragment<wmma::matrix_a, 16, 16, 16, __half, wmma::row_major> a;
             wmma::load_matrix_sync(a, ks + 16 * warp * kKLd + 16 * kk, kKLd);
 #pragma unroll
             for (int n = 0; n < 4; ++n) {
-                wmma::fragment<wmma::matrix_b, 16, 16, 16, __nv_bfloat16, wmma::col_major> bq;
+                wmma::fragment<wmma::matrix_b, 16, 16, 16, __half, wmma::col_major> bq;
                 wmma::load_matrix_sync(bq, qs + 16 * n * kQLd + 16 * kk, kQLd);
                 wmma::mma_sync(acc[n], a, bq, acc[n]);
             }
         }
+        __syncthreads();                             // every warp's products read the keys
 #pragma unroll
         for (int n = 0; n < 4; ++n)
             wmma::store_matrix_sync(ss + 16 * warp * kSLd + 16 * n, acc[n], kSLd, wmma::mem_row_major);
