@@ -17,15 +17,15 @@
 //                       to fp16 in shared memory by the hardware conversions (code x e4m3
 //                       scale has at most 5 significant bits), q in fp16 after an exact
 //                       power-of-two scale per head (folded into the head's weight), K . Q^T on
-//                       the tensor cores (wmma fp16, fp32 accumulation), then the ReLU-weighted
-//                       head sum per position.
+//                       the tensor cores (mma.sync m16n8k16 fp16, fp32 accumulation; a warp
+//                       takes 32 positions x 32 heads and keeps its q fragments in registers for
+//                       the run), then the ReLU-weighted head sum per position from the
+//                       accumulators.
 //   index_topk_kernel   one thread-block cluster of 8 CTAs per query, each CTA an eighth of
 //                       the positions: an 8-pass 4-bit radix select of the k-th largest score
 //                       (digit counts exchanged through distributed shared memory), then the
 //                       selected positions written in ascending order (ties at the threshold
 //                       go to the lowest positions), mapped to pool rows.
-#include <mma.h>
-
 #include "abi_common.h"
 #include "common.cuh"
 
@@ -40,10 +40,6 @@ constexpr int kIRow = NVFP4KV_INDEX_ROW_BYTES;      // 72
 // 16 x 16 fragment load in the same banks.
 constexpr int kQLd = kIDim + 8;                     // fp16 elements
 constexpr int kKLd = kIDim + 8;
-constexpr int kSLd = kIHeads + 4;                   // fp32 elements
-// The fp32 head scores of a tile reuse the key tile's space once the products are done (the
-// same 34,816 bytes), so four blocks fit on an SM.
-static_assert(kITile * kSLd * 4 == kITile * kKLd * 2, "score staging aliases the key tile");
 constexpr int kScoreSmem = kIHeads * kQLd * 2 + kITile * kKLd * 2;   // 52224
 
 struct ScoreParams {
@@ -120,6 +116,22 @@ __device__ __forceinline__ void store_key_part(const KeyPart& k, uint32_t* dst) 
     }
 }
 
+// Tensor-core fragments of mma.sync m16n8k16 (fp16 in, fp32 accumulation): A 16 x 16 row-major
+// from four 8 x 8 shared-memory matrices, B 16 x 8 (k x n) from two, stored n-major.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t (&r)[2]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
+}
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+                 "{%8, %9}, {%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
 // Block = (entry b, a run of kTilesPerBlock position tiles): the entry's q and weights are
 // loaded once, and each tile's key bytes are loaded a tile ahead of their dequantisation.
 constexpr int kTilesPerBlock = 8;
@@ -128,15 +140,16 @@ __global__ void __launch_bounds__(256) index_score_kernel(const ScoreParams p, i
     extern __shared__ __align__(128) uint8_t smem[];
     __half* qs = reinterpret_cast<__half*>(smem);                            // [64 heads][kQLd] fp16
     __half* ks = qs + kIHeads * kQLd;                                        // [128 positions][kKLd] fp16
-    float* ss = reinterpret_cast<float*>(ks);                                 // [128 positions][kSLd], after the products
     __shared__ float ws[kIHeads];
+    __shared__ float red[2 * kITile];                // per head half: the tile's partial sums
+    __shared__ uint8_t tile_ok[kITile];              // position on a page of the pool
     const int runs = (p.tiles + kTilesPerBlock - 1) / kTilesPerBlock;
     const int b = blockIdx.x / runs, run = blockIdx.x % runs;
     const int L = clamp_len(p.seq_lens, b, p.max_seq_len, err);
     const int t0 = run * kTilesPerBlock;
     const int t1 = min(min(t0 + kTilesPerBlock, p.tiles), (L + kITile - 1) / kITile);
     if (t0 >= t1) return;                            // the whole block: nothing visible here
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     {
         // q in fp16 for the fp16 tensor-core product: head h is scaled by 2^(10 - e_h), e_h =
         // floor(log2 max|q_h|), which is exact and keeps the head inside fp16's range, and its
@@ -174,43 +187,74 @@ __global__ void __launch_bounds__(256) index_score_kernel(const ScoreParams p, i
     const int tok = tid >> 1, half = tid & 1;
     uint32_t* kdst = reinterpret_cast<uint32_t*>(ks + tok * kKLd + 64 * half);
     KeyPart next = load_key_part(p, b, t0 * kITile + tok, L, half);
-    using namespace nvcuda;
+    __syncthreads();                                 // q and the weights are in shared memory
+    // Warp w: positions 32 (w & 3) .. +31 (two m-tiles of 16) x heads 32 (w >> 2) .. +31 (four
+    // n-tiles of 8): the key tile is read twice per tile in all (not once per warp), and the
+    // warp's q fragments (B of m16n8k16, all 128 dims) and weights stay in registers for the run.
+    const int pb = warp & 3, hq = warp >> 2;
+    uint32_t qf[kIDim / 16][4][2];
+#pragma unroll
+    for (int kk = 0; kk < kIDim / 16; ++kk)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+            ldsm_x2(smem_u32(qs + (32 * hq + 8 * nt + (lane & 7)) * kQLd + 16 * kk + 8 * ((lane >> 3) & 1)),
+                    qf[kk][nt]);
+    float wv[4][2];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+        wv[nt][0] = ws[32 * hq + 8 * nt + 2 * (lane & 3)];
+        wv[nt][1] = ws[32 * hq + 8 * nt + 2 * (lane & 3) + 1];
+    }
 #pragma unroll 1
     for (int tile = t0; tile < t1; ++tile) {
         const KeyPart cur = next;
-        __syncthreads();                             // the previous tile's keys are consumed
+        __syncthreads();                             // the previous tile's keys and sums are consumed
         store_key_part(cur, kdst);
+        if (half == 0) tile_ok[tok] = cur.ok;
         if (tile + 1 < t1) next = load_key_part(p, b, (tile + 1) * kITile + tok, L, half);
         __syncthreads();
-        // warp w: positions 16w .. 16w+15 against all 64 heads
-        wmma::fragment<wmma::accumulator, 16, 16, 16, float> acc[4];
+        // thread l of the warp ends with positions 32 pb + 16 mt + l/4 (+8) x heads
+        // 32 hq + 8 nt + 2 (l % 4) (+1); the ReLU-weighted sum over its heads, then the quad's
+        float acc[2][4][4];
 #pragma unroll
-        for (int n = 0; n < 4; ++n) wmma::fill_fragment(acc[n], 0.0f);
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[mt][nt][j] = 0.0f;
 #pragma unroll
         for (int kk = 0; kk < kIDim / 16; ++kk) {
-            wmma::fragment<wmma::matrix_a, 16, 16, 16, __half, wmma::row_major> a;
-            wmma::load_matrix_sync(a, ks + 16 * warp * kKLd + 16 * kk, kKLd);
 #pragma unroll
-            for (int n = 0; n < 4; ++n) {
-                wmma::fragment<wmma::matrix_b, 16, 16, 16, __half, wmma::col_major> bq;
-                wmma::load_matrix_sync(bq, qs + 16 * n * kQLd + 16 * kk, kQLd);
-                wmma::mma_sync(acc[n], a, bq, acc[n]);
+            for (int mt = 0; mt < 2; ++mt) {
+                uint32_t af[4];
+                ldsm_x4(smem_u32(ks + (32 * pb + 16 * mt + (lane & 15)) * kKLd + 16 * kk + 8 * (lane >> 4)), af);
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt) mma_16816(acc[mt][nt], af, qf[kk][nt]);
             }
         }
-        __syncthreads();                             // every warp's products read the keys
 #pragma unroll
-        for (int n = 0; n < 4; ++n)
-            wmma::store_matrix_sync(ss + 16 * warp * kSLd + 16 * n, acc[n], kSLd, wmma::mem_row_major);
-        __syncwarp();
-        // thread (position tid >> 1, heads 32 half .. +32): the ReLU-weighted sum, halves combined
-        float sum = 0.0f;
-#pragma unroll 8
-        for (int h = 0; h < 32; ++h)
-            sum = fmaf(ws[32 * half + h], fmaxf(ss[tok * kSLd + 32 * half + h], 0.0f), sum);
-        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
-        const int pos = tile * kITile + tok;
-        if (half == 0 && pos < L)
-            p.scores[static_cast<int64_t>(b) * p.tiles * kITile + pos] = cur.ok ? sum : -INFINITY;
+        for (int mt = 0; mt < 2; ++mt) {
+            float lo = 0.0f, hi = 0.0f;
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt) {
+                lo = fmaf(wv[nt][0], fmaxf(acc[mt][nt][0], 0.0f), fmaf(wv[nt][1], fmaxf(acc[mt][nt][1], 0.0f), lo));
+                hi = fmaf(wv[nt][0], fmaxf(acc[mt][nt][2], 0.0f), fmaf(wv[nt][1], fmaxf(acc[mt][nt][3], 0.0f), hi));
+            }
+            lo += __shfl_xor_sync(0xFFFFFFFFu, lo, 1);
+            lo += __shfl_xor_sync(0xFFFFFFFFu, lo, 2);
+            hi += __shfl_xor_sync(0xFFFFFFFFu, hi, 1);
+            hi += __shfl_xor_sync(0xFFFFFFFFu, hi, 2);
+            if ((lane & 3) == 0) {
+                red[hq * kITile + 32 * pb + 16 * mt + (lane >> 2)] = lo;
+                red[hq * kITile + 32 * pb + 16 * mt + (lane >> 2) + 8] = hi;
+            }
+        }
+        __syncthreads();
+        if (tid < kITile) {
+            const float sum = red[tid] + red[kITile + tid];
+            const int pos = tile * kITile + tid;
+            if (pos < L) p.scores[static_cast<int64_t>(b) * p.tiles * kITile + pos] = tile_ok[tid] ? sum : -INFINITY;
+        }
     }
 }
 

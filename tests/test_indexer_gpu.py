@@ -75,12 +75,16 @@ def _case(rt, lens, pages, seed, topk=2048, missing=()):
     return pool_np, tables, q, w, sl, rows.cpu().numpy(), counts.cpu().numpy(), gpu_scores, ref_scores
 
 
-@pytest.mark.parametrize("lens,missing", [([6000, 2048, 777, 4097], ()), ([9000, 3000], ((0, 5), (1, 2)))])
+@pytest.mark.parametrize("lens,missing", [([6000, 2048, 777, 4097], ()), ([9000, 3000], ((0, 5), (1, 2))),
+                                          ([0, 3, 2049, 10000], ())])
 def test_index_topk_scores_and_selection(rt, lens, missing):
     pages = 200
     pool_np, tables, q, w, sl, rows, counts, gs, rs = _case(rt, lens, pages, seed=sum(lens), missing=missing)
     topk = 2048
     for b, n in enumerate(lens):
+        if n == 0:                                                      # nothing visible: no rows
+            assert counts[b] == 0 and (rows[b] == -1).all()
+            continue
         ref = rs[b]
         got = gs[b, :n]
         fin = np.isfinite(ref)
