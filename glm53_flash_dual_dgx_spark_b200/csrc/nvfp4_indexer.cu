@@ -13,19 +13,20 @@
 // for every visible position s < seq_len[b], then the topk largest.
 //
 // Kernels:
-//   index_score_kernel  one block per (query, run of 8 128-position tiles): keys dequantised exactly
-//                       to fp16 in shared memory by the hardware conversions (code x e4m3
-//                       scale has at most 5 significant bits), q in fp16 after an exact
-//                       power-of-two scale per head (folded into the head's weight), K . Q^T on
-//                       the tensor cores (mma.sync m16n8k16 fp16, fp32 accumulation; a warp
-//                       takes 32 positions x 32 heads and keeps its q fragments in registers for
-//                       the run), then the ReLU-weighted head sum per position from the
-//                       accumulators.
+//   index_score_kernel  one block per (query, run of its 128-position tiles), one wave over the
+//                       SMs: whole pages of key rows bulk-copied into a ring, each tile of 128
+//                       keys the NVFP4 A operand of tcgen05 block-scaled fp4 MMAs (its e4m3
+//                       scales as the A scale factors) against q written as four NVFP4 terms
+//                       (after an exact power-of-two scale per head, folded into the head's
+//                       weight), fp32 accumulators in TMEM, then the ReLU-weighted head sum per
+//                       position from the accumulators.
 //   index_topk_kernel   one thread-block cluster of 8 CTAs per query, each CTA an eighth of
 //                       the positions: an 8-pass 4-bit radix select of the k-th largest score
 //                       (digit counts exchanged through distributed shared memory), then the
 //                       selected positions written in ascending order (ties at the threshold
 //                       go to the lowest positions), mapped to pool rows.
+#include <algorithm>
+
 #include "abi_common.h"
 #include "common.cuh"
 
@@ -36,11 +37,6 @@ constexpr int kITile = 128;                         // positions per score block
 constexpr int kIHeads = 64;                         // indexer heads
 constexpr int kIDim = NVFP4KV_INDEX_DIM;            // 128
 constexpr int kIRow = NVFP4KV_INDEX_ROW_BYTES;      // 72
-// Shared-memory row strides padded by 16 bytes: rows 256 bytes apart would put every row of a
-// 16 x 16 fragment load in the same banks.
-constexpr int kQLd = kIDim + 8;                     // fp16 elements
-constexpr int kKLd = kIDim + 8;
-constexpr int kScoreSmem = kIHeads * kQLd * 2 + kITile * kKLd * 2;   // 52224
 
 struct ScoreParams {
     const __nv_bfloat16* q;       // [batch][heads][128], row strides below
@@ -53,6 +49,7 @@ struct ScoreParams {
     int64_t tables_stride;
     const int32_t* seq_lens;
     int page_shift, max_seq_len, tiles;
+    int runs;                     // blocks per entry
     float* scores;                // [batch][tiles * 128]
 };
 
@@ -73,188 +70,364 @@ __device__ __forceinline__ int64_t index_row(const int32_t* tables, int64_t stri
     return (static_cast<int64_t>(pg) << shift) | (pos & ((1 << shift) - 1));
 }
 
-// One thread's share of a key tile: position tid >> 1, half tid & 1 (64 elements = 4 blocks):
-// 32 code bytes and 4 scale bytes, loaded ahead of their use.
-struct KeyPart {
-    uint2 c[4];
-    uint32_t s;
-    bool ok;
-};
+// ------------------------------------------------------------------ scores (tcgen05)
+// A 72-byte key row already is NVFP4 (64 code bytes, one e4m3 scale per 16 dims), so a tile of
+// 128 keys is the A operand of tcgen05.mma kind::mxf4nvf4.block_scale.block16 with its scales
+// as the A scale factors, and q is written as four NVFP4 terms on the N side, as the attention
+// kernel does for its queries: column h of the accumulator holds terms 1 + 3 of head h, column
+// 64 + h terms 2 + 4 (two passes of N = 128).  Each head is first scaled by 2^-e_h (exact, so
+// that its largest |q| lies in [2^10, 2^11)); 2^e_h goes into the head's weight, since
+// max(c x, 0) = c max(x, 0) for c > 0.
+//
+// Warps (512 threads): 0 loads (page runs of the pool, bulk copies into a ring of raw tiles;
+// the run's page ids staged in shared memory a window at a time, so no copy waits on a table
+// load), 1 issues the MMAs, 2 owns the TMEM allocation, 4-7 rewrite each raw tile into the
+// 128-byte swizzled operand layout and its scales into TMEM (warp w: sub-partition w & 3),
+// 8-15 read a finished tile's 128 accumulator columns (thread = key position) and write the
+// ReLU-weighted head sum: warps 8-11 the tiles of accumulator 0, 12-15 those of accumulator 1,
+// so each set has two tile periods per tile.  Warps 4-11 quantise q at the start.  Every wait
+// is bounded (common.cuh).
+constexpr int kSStages = 6;                                  // raw key tiles in flight
+constexpr int kKeyTileBytes = kITile * kIRow;                // 9216
+constexpr int kSThreads = 512;
+constexpr int kSLoadWarp = 0, kSMmaWarp = 1, kSAllocWarp = 2, kSConvWarp0 = 4, kSEpiWarp0 = 8;
+constexpr int kSPrepBar = 1;                                 // named barrier of warps 4-15
+constexpr int kPgWin = 1024;                                 // page ids the loader stages at a time
+// Registers moved between warpgroups at run time (setmaxnreg; launched with 128 a thread): the
+// epilogue keeps the 64 head weights in registers.
+constexpr uint32_t kSRegsCtl = 64, kSRegsConv = 96, kSRegsEpi = 168;
+static_assert(128 * (kSRegsCtl + kSRegsConv + 2 * kSRegsEpi) <= kSThreads * 128, "register split within the launch");
+constexpr int SS_QB = 0;                                     // Q terms: 2 passes x [128 rows x 128 B], 64 B used
+constexpr int SS_A = SS_QB + 2 * 16384;                      // 2 x key codes [128 rows x 128 B], 64 B used
+constexpr int SS_STG = SS_A + 2 * 16384;                     // kSStages x [128 rows x 72 B] as copied
+constexpr int SS_QSF = SS_STG + kSStages * kKeyTileBytes;    // [2 passes][128 rows][8] Q-term scales
+constexpr int SS_WQ = SS_QSF + 2 * 128 * 8;                  // 64 f32: w[h] 2^e_h
+constexpr int SS_PG = SS_WQ + 256;                           // kPgWin i32: the loader's page ids
+constexpr int SS_FLAGS = SS_PG + kPgWin * 4;                 // [0] TMEM base, [1] abort
+constexpr int SS_BARS = SS_FLAGS + 16;
+constexpr int SB_FULL = 0;                                   // [stages] raw tile landed
+constexpr int SB_FREE = SB_FULL + kSStages;                  // [stages] converters done with it
+constexpr int SB_AFULL = SB_FREE + kSStages;                 // [2] operand tile + its scales ready
+constexpr int SB_AFREE = SB_AFULL + 2;                       // [2] MMAs done reading them
+constexpr int SB_DFULL = SB_AFREE + 2;                       // [2] accumulator complete
+constexpr int SB_DFREE = SB_DFULL + 2;                       // [2] accumulator read
+constexpr int SB_DRAIN = SB_DFREE + 2;                       // every MMA complete (before TMEM is freed)
+constexpr int kSBars = SB_DRAIN + 1;
+constexpr int kScoreSmem = SS_BARS + kSBars * 8 + 1024;      // slack to align the base
+static_assert(kScoreSmem <= 232448, "shared memory budget");
+constexpr uint32_t kSTD = 0;        // 2 x 128 columns: accumulators
+constexpr uint32_t kSTSFA = 256;    // 2 x 8 columns: key scales (column 4 kk + q: word kk of row 32 q + lane)
+constexpr uint32_t kSTSFB = 272;    // 16 columns: Q-term scales (8 pass + 4 kk + q)
+constexpr uint32_t kSTCols = 512;
+static_assert(kIDim == 2 * 64 && kIRow == kIDim / 2 + kIDim / 16, "a key row: two K-chunks of 64 codes, then their scales");
 
-__device__ __forceinline__ KeyPart load_key_part(const ScoreParams& p, int b, int pos, int L, int half) {
-    KeyPart k{};
-    const int64_t row = pos < L ? index_row(p.tables, p.tables_stride, b, pos, p.page_shift, p.num_pages) : -1;
-    k.ok = row >= 0;
-    if (k.ok) {
-        const uint8_t* src = p.pool + row * kIRow;
-#pragma unroll
-        for (int blk = 0; blk < 4; ++blk) k.c[blk] = *reinterpret_cast<const uint2*>(src + 32 * half + 8 * blk);
-        k.s = *reinterpret_cast<const uint32_t*>(src + 64 + 4 * half);
-    }
-    return k;
+// Four floats from shared memory, issued where written (not hoisted out of a loop).
+__device__ __forceinline__ float4 lds_f32x4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
 }
 
-// Dequantise a key part into the fp16 tile row with the hardware conversions (e2m1 pair ->
-// f16x2, e4m3 pair -> f16x2, one f16x2 multiply): code x scale is exact in fp16 (at most 5
-// significant bits, magnitudes 2^-10 .. 2688), zeros for a masked position.
-__device__ __forceinline__ void store_key_part(const KeyPart& k, uint32_t* dst) {
-    if (!k.ok) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) dst[j] = 0u;
-        return;
-    }
-    const uint32_t s01 = e4m3x2_to_f16x2(static_cast<uint16_t>(k.s & 0xFFFFu));
-    const uint32_t s23 = e4m3x2_to_f16x2(static_cast<uint16_t>(k.s >> 16));
-    const uint32_t sb[4] = {(s01 & 0xFFFFu) * 0x10001u, (s01 >> 16) * 0x10001u, (s23 & 0xFFFFu) * 0x10001u,
-                            (s23 >> 16) * 0x10001u};
-#pragma unroll
-    for (int blk = 0; blk < 4; ++blk) {
-        const uint32_t w2[2] = {k.c[blk].x, k.c[blk].y};
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            dst[8 * blk + j] = hmul2_u32(e2m1x2_to_f16x2((w2[j >> 2] >> (8 * (j & 3))) & 0xFFu), sb[blk]);
-    }
-}
-
-// Tensor-core fragments of mma.sync m16n8k16 (fp16 in, fp32 accumulation): A 16 x 16 row-major
-// from four 8 x 8 shared-memory matrices, B 16 x 8 (k x n) from two, stored n-major.
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t (&r)[2]) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
-}
-__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
-                 "{%8, %9}, {%0, %1, %2, %3};"
-                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
-}
-
-// Block = (entry b, a run of kTilesPerBlock position tiles): the entry's q and weights are
-// loaded once, and each tile's key bytes are loaded a tile ahead of their dequantisation.
-constexpr int kTilesPerBlock = 8;
-
-__global__ void __launch_bounds__(256) index_score_kernel(const ScoreParams p, int32_t* err) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __half* qs = reinterpret_cast<__half*>(smem);                            // [64 heads][kQLd] fp16
-    __half* ks = qs + kIHeads * kQLd;                                        // [128 positions][kKLd] fp16
-    __shared__ float ws[kIHeads];
-    __shared__ float red[2 * kITile];                // per head half: the tile's partial sums
-    __shared__ uint8_t tile_ok[kITile];              // position on a page of the pool
-    const int runs = (p.tiles + kTilesPerBlock - 1) / kTilesPerBlock;
-    const int b = blockIdx.x / runs, run = blockIdx.x % runs;
-    const int L = clamp_len(p.seq_lens, b, p.max_seq_len, err);
-    const int t0 = run * kTilesPerBlock;
-    const int t1 = min(min(t0 + kTilesPerBlock, p.tiles), (L + kITile - 1) / kITile);
-    if (t0 >= t1) return;                            // the whole block: nothing visible here
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    {
-        // q in fp16 for the fp16 tensor-core product: head h is scaled by 2^(10 - e_h), e_h =
-        // floor(log2 max|q_h|), which is exact and keeps the head inside fp16's range, and its
-        // weight by 2^(e_h - 10) (max(c x, 0) = c max(x, 0) for c > 0).  Four threads per head,
-        // 32 dims each.
-        const int h = tid >> 2, c0 = 32 * (tid & 3);
-        const __nv_bfloat16* src = p.q + b * p.q_sb + h * p.q_sh + c0;
-        uint4 v[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = ldg_nc_v4(src + 8 * j);
-        float x[32];
-        float am = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint32_t w4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                x[8 * j + 2 * t] = __uint_as_float(w4[t] << 16);
-                x[8 * j + 2 * t + 1] = __uint_as_float(w4[t] & 0xFFFF0000u);
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < 32; ++j) am = fmaxf(am, fabsf(x[j]));
-        am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, 1));
-        am = fmaxf(am, __shfl_xor_sync(0xFFFFFFFFu, am, 2));
-        const int eb = static_cast<int>((__float_as_uint(am) >> 23) & 0xFFu);   // biased exponent
-        const int e = (eb > 0 && eb < 255) ? eb - 127 : 0;
-        const int sh = max(-100, min(100, 10 - e));
-        const float mul = __uint_as_float(static_cast<uint32_t>(127 + sh) << 23);   // 2^sh
-        uint32_t* dst = reinterpret_cast<uint32_t*>(qs + h * kQLd + c0);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) dst[j] = pack_half2(x[2 * j] * mul, x[2 * j + 1] * mul);
-        if ((tid & 3) == 0) ws[h] = __ldg(p.w + b * p.w_sb + h) * __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
-    }
-    const int tok = tid >> 1, half = tid & 1;
-    uint32_t* kdst = reinterpret_cast<uint32_t*>(ks + tok * kKLd + 64 * half);
-    KeyPart next = load_key_part(p, b, t0 * kITile + tok, L, half);
-    __syncthreads();                                 // q and the weights are in shared memory
-    // Warp w: positions 32 (w & 3) .. +31 (two m-tiles of 16) x heads 32 (w >> 2) .. +31 (four
-    // n-tiles of 8): the key tile is read twice per tile in all (not once per warp), and the
-    // warp's q fragments (B of m16n8k16, all 128 dims) and weights stay in registers for the run.
-    const int pb = warp & 3, hq = warp >> 2;
-    uint32_t qf[kIDim / 16][4][2];
-#pragma unroll
-    for (int kk = 0; kk < kIDim / 16; ++kk)
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt)
-            ldsm_x2(smem_u32(qs + (32 * hq + 8 * nt + (lane & 7)) * kQLd + 16 * kk + 8 * ((lane >> 3) & 1)),
-                    qf[kk][nt]);
-    float wv[4][2];
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-        wv[nt][0] = ws[32 * hq + 8 * nt + 2 * (lane & 3)];
-        wv[nt][1] = ws[32 * hq + 8 * nt + 2 * (lane & 3) + 1];
-    }
+// q of entry b -> four NVFP4 terms in the B-operand image (term tt: pass tt >> 1, row
+// 64 (tt & 1) + h, K-major, 128-byte swizzle), their scales [pass][row][8], and w[h] 2^e_h.
+// Warps 4-11, eight lanes per head (lane j: dims 16 j .. 16 j + 15), four heads per warp and
+// round.
+__device__ __forceinline__ void index_q_prep(const ScoreParams& p, int b, uint8_t* smem, int wi, int lane) {
+    const int j = lane & 7;
 #pragma unroll 1
-    for (int tile = t0; tile < t1; ++tile) {
-        const KeyPart cur = next;
-        __syncthreads();                             // the previous tile's keys and sums are consumed
-        store_key_part(cur, kdst);
-        if (half == 0) tile_ok[tok] = cur.ok;
-        if (tile + 1 < t1) next = load_key_part(p, b, (tile + 1) * kITile + tok, L, half);
-        __syncthreads();
-        // thread l of the warp ends with positions 32 pb + 16 mt + l/4 (+8) x heads
-        // 32 hq + 8 nt + 2 (l % 4) (+1); the ReLU-weighted sum over its heads, then the quad's
-        float acc[2][4][4];
+    for (int it = 0; it < 2; ++it) {
+        const int h = 32 * it + 4 * wi + (lane >> 3);
+        const __nv_bfloat16* src = p.q + b * p.q_sb + h * p.q_sh + 16 * j;
+        const uint4 u0 = ldg_nc_v4(src), u1 = ldg_nc_v4(src + 8);
+        const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+        float x[16];
+        float amax = 0.0f;
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-            for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[mt][nt][j] = 0.0f;
-#pragma unroll
-        for (int kk = 0; kk < kIDim / 16; ++kk) {
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt) {
-                uint32_t af[4];
-                ldsm_x4(smem_u32(ks + (32 * pb + 16 * mt + (lane & 15)) * kKLd + 16 * kk + 8 * (lane >> 4)), af);
-#pragma unroll
-                for (int nt = 0; nt < 4; ++nt) mma_16816(acc[mt][nt], af, qf[kk][nt]);
-            }
+        for (int k = 0; k < 8; ++k) {
+            x[2 * k] = __uint_as_float(w8[k] << 16);
+            x[2 * k + 1] = __uint_as_float(w8[k] & 0xFFFF0000u);
+            amax = fmaxf(amax, fmaxf(fabsf(x[2 * k]), fabsf(x[2 * k + 1])));
         }
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-            float lo = 0.0f, hi = 0.0f;
+        for (int off = 4; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, off));
+        const int eb = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu);
+        int e = (eb > 0 && eb < 255) ? eb - 127 - 10 : 0;
+        e = max(-100, min(100, e));
+        const float mul = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);   // 2^-e, exact
 #pragma unroll
-            for (int nt = 0; nt < 4; ++nt) {
-                lo = fmaf(wv[nt][0], fmaxf(acc[mt][nt][0], 0.0f), fmaf(wv[nt][1], fmaxf(acc[mt][nt][1], 0.0f), lo));
-                hi = fmaf(wv[nt][0], fmaxf(acc[mt][nt][2], 0.0f), fmaf(wv[nt][1], fmaxf(acc[mt][nt][3], 0.0f), hi));
+        for (int k = 0; k < 16; ++k) x[k] *= mul;
+#pragma unroll
+        for (int tt = 0; tt < 4; ++tt) {
+            float am = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) am = fmaxf(am, fabsf(x[k]));
+            const uint8_t sb = am > 0.0f ? f32_to_e4m3(am * (1.0f / 6.0f)) : static_cast<uint8_t>(0);
+            const float sf = e4m3_to_f32(sb);
+            const float inv = sf > 0.0f ? rcp_approx(sf) : 0.0f;
+            uint32_t wlo = 0, whi = 0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const uint32_t byte = f32x2_to_e2m1x2(x[2 * k] * inv, x[2 * k + 1] * inv);
+                if (k < 4) wlo |= byte << (8 * k);
+                else whi |= byte << (8 * (k - 4));
+                const uint32_t dq = e2m1x2_to_f16x2(byte);
+                x[2 * k] -= __half2float(__ushort_as_half(static_cast<unsigned short>(dq & 0xFFFFu))) * sf;
+                x[2 * k + 1] -= __half2float(__ushort_as_half(static_cast<unsigned short>(dq >> 16))) * sf;
             }
-            lo += __shfl_xor_sync(0xFFFFFFFFu, lo, 1);
-            lo += __shfl_xor_sync(0xFFFFFFFFu, lo, 2);
-            hi += __shfl_xor_sync(0xFFFFFFFFu, hi, 1);
-            hi += __shfl_xor_sync(0xFFFFFFFFu, hi, 2);
-            if ((lane & 3) == 0) {
-                red[hq * kITile + 32 * pb + 16 * mt + (lane >> 2)] = lo;
-                red[hq * kITile + 32 * pb + 16 * mt + (lane >> 2) + 8] = hi;
+            const int ps = tt >> 1, R = 64 * (tt & 1) + h, c = j >> 1;
+            *reinterpret_cast<uint2*>(smem + SS_QB + ps * 16384 + (R >> 3) * 1024 + (R & 7) * 128 +
+                                      ((c ^ (R & 7)) << 4) + 8 * (j & 1)) = make_uint2(wlo, whi);
+            smem[SS_QSF + (ps * 128 + R) * 8 + j] = sb;
+        }
+        if (j == 0)
+            reinterpret_cast<float*>(smem + SS_WQ)[h] = __ldg(p.w + b * p.w_sb + h) * ldexpf(1.0f, e);
+    }
+}
+
+// Block = (entry b, run r of its tiles): the tiles of visible positions are cut into p.runs
+// equal runs, so a batch of B entries fills about B x runs SMs in one wave.
+__global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScoreParams p, int32_t* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    const uint32_t sbase = smem_u32(smem);
+    const int b = blockIdx.x / p.runs, run = blockIdx.x % p.runs;
+    const int L = clamp_len(p.seq_lens, b, p.max_seq_len, err);
+    const int tiles_b = (L + kITile - 1) / kITile;
+    const int per = (tiles_b + p.runs - 1) / p.runs;
+    const int t0 = run * per, t1 = min(t0 + per, tiles_b);
+    if (t0 >= t1) return;                            // the whole block: nothing visible here
+    const int n = t1 - t0;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    volatile int* flags = reinterpret_cast<volatile int*>(smem + SS_FLAGS);
+    volatile int* abort_flag = flags + 1;
+    auto bar = [&](int i) -> uint32_t { return sbase + SS_BARS + 8 * i; };
+    if (tid == 0) {
+        for (int s = 0; s < kSStages; ++s) {
+            mbar_init(bar(SB_FULL + s), 1);
+            mbar_init(bar(SB_FREE + s), 4);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(bar(SB_AFULL + a), 4);
+            mbar_init(bar(SB_AFREE + a), 1);
+            mbar_init(bar(SB_DFULL + a), 1);
+            mbar_init(bar(SB_DFREE + a), 4);
+        }
+        mbar_init(bar(SB_DRAIN), 1);
+        flags[1] = 0;
+        mbar_fence_init();
+    }
+    if (warp == kSAllocWarp) {
+        tmem_alloc(sbase + SS_FLAGS, kSTCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = static_cast<uint32_t>(flags[0]);
+
+    // each role's code follows its own register budget change (setmaxnreg), so the compiler
+    // allocates every role within its budget
+    if (warp < kSConvWarp0) {
+    warpgroup_reg_dealloc<kSRegsCtl>();
+    if (warp == kSLoadWarp) {
+        // ============================================================ loads
+        // a tile is 128 / page runs of one page each (pages of <= 128 positions) or 128 rows
+        // of one page; runs of pages that are missing or lie wholly past the visible end are
+        // not copied (their positions score -inf or are not written)
+        const int run_rows = p.page_shift >= 7 ? kITile : (1 << p.page_shift);
+        const int runs_per_tile = kITile / run_rows;
+        const uint32_t run_bytes = static_cast<uint32_t>(run_rows * kIRow);
+        int* pgw = reinterpret_cast<int*>(smem + SS_PG);   // page ids of pages wbase .. wbase + kPgWin - 1
+        const int last_page = (min(t1 * kITile, L) - 1) >> p.page_shift;
+        int wbase = -2 * kPgWin;
+        int issued = 0;
+#pragma unroll 1
+        for (int j = 0; j < n; ++j) {
+            const int s = j % kSStages;
+            if (j >= kSStages) {
+                const bool ok = mbar_wait(bar(SB_FREE + s), ((j / kSStages) - 1) & 1, abort_flag, err);
+                if (!ok || *abort_flag) break;
+                fence_proxy_async_smem();
+            }
+            const int pos0 = (t0 + j) * kITile;
+            const int pfirst = pos0 >> p.page_shift, plast = min(pos0 + kITile, L) - 1 >> p.page_shift;
+            if (pfirst < wbase || plast >= wbase + kPgWin) {   // the tile's pages: one window (<= 64 pages)
+                __syncwarp();
+                wbase = pfirst;
+                const int cnt = min(kPgWin, last_page - wbase + 1);
+                for (int k = lane; k < cnt; k += 32) pgw[k] = __ldg(p.tables + b * p.tables_stride + wbase + k);
+                __syncwarp();
+            }
+            auto run_page = [&](int pos) -> int {   // page id of a visible position, -1 off the pool
+                const int pg = pgw[(pos >> p.page_shift) - wbase];
+                return (pg < 0 || pg >= p.num_pages) ? -1 : pg;
+            };
+            uint32_t bytes = 0;
+            for (int r = lane; r < runs_per_tile; r += 32) {
+                const int pos = pos0 + r * run_rows;
+                if (pos < L && run_page(pos) >= 0) bytes += run_bytes;
+            }
+            bytes = __reduce_add_sync(0xFFFFFFFFu, bytes);
+            if (lane == 0) mbar_arrive_expect_tx(bar(SB_FULL + s), bytes);
+            __syncwarp();
+            for (int r = lane; r < runs_per_tile; r += 32) {
+                const int pos = pos0 + r * run_rows;
+                if (pos >= L) continue;
+                const int pg = run_page(pos);
+                if (pg >= 0) {
+                    const int64_t row = (static_cast<int64_t>(pg) << p.page_shift) | (pos & ((1 << p.page_shift) - 1));
+                    bulk_copy_g2s(sbase + SS_STG + s * kKeyTileBytes + r * run_bytes, p.pool + row * kIRow, run_bytes,
+                                  bar(SB_FULL + s));
+                }
+            }
+            issued = j + 1;
+        }
+        // copies in flight land before the CTA can exit
+        for (int j = issued > kSStages ? issued - kSStages : 0; j < issued; ++j)
+            mbar_drain_wait(bar(SB_FULL + j % kSStages), (j / kSStages) & 1);
+        __syncwarp();
+    } else if (warp == kSMmaWarp) {
+        // ============================================================ MMA issue
+        constexpr uint32_t idq = idesc_fp4_f32(kITile, 128);
+        const uint64_t dq = smem_desc_sw128(sbase + SS_QB, 16, 1024);
+        const uint64_t da = smem_desc_sw128(sbase + SS_A, 16, 1024);
+#pragma unroll 1
+        for (int j = 0; j < n; ++j) {
+            const int a = j & 1;
+            if (!mbar_wait(bar(SB_AFULL + a), (j >> 1) & 1, abort_flag, err)) break;
+            if (j >= 2 && !mbar_wait(bar(SB_DFREE + a), ((j >> 1) - 1) & 1, abort_flag, err)) break;
+            tc_fence_after();
+            if (elect_one()) {
+#pragma unroll
+                for (int ps = 0; ps < 2; ++ps)
+#pragma unroll
+                    for (int kk = 0; kk < 2; ++kk)
+                        tc_mma_fp4(tmem + kSTD + 128 * a, da + ((a * 16384 + kk * 32) >> 4),
+                                   dq + ((ps * 16384 + kk * 32) >> 4), idq, (ps | kk) != 0,
+                                   tmem + kSTSFA + 8 * a + 4 * kk, tmem + kSTSFB + 8 * ps + 4 * kk);
+                tc_commit(bar(SB_AFREE + a));
+                tc_commit(bar(SB_DFULL + a));
+            }
+            __syncwarp();
+        }
+        // every MMA of this CTA completes before its TMEM is freed, on the abort path too
+        if (elect_one()) tc_commit(bar(SB_DRAIN));
+        __syncwarp();
+        mbar_drain_wait(bar(SB_DRAIN), 0);
+    }
+    } else if (warp < kSEpiWarp0) {
+        warpgroup_reg_dealloc<kSRegsConv>();
+        index_q_prep(p, b, smem, warp - kSConvWarp0, lane);
+        fence_proxy_async_smem();                    // the Q terms are read by the tensor core
+        named_bar_sync(kSPrepBar, 12 * 32);
+        const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+        {
+            // ======================================================== operand tiles
+            {   // Q-term scales into this sub-partition: column 8 ps + 4 kk + q = word kk of row 32 q + lane
+                uint32_t v[16];
+#pragma unroll
+                for (int ps = 0; ps < 2; ++ps)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const uint2 w = *reinterpret_cast<const uint2*>(smem + SS_QSF + (ps * 128 + 32 * q + lane) * 8);
+                        v[8 * ps + q] = w.x;
+                        v[8 * ps + 4 + q] = w.y;
+                    }
+                tmem_st16(tmem + lane_base + kSTSFB, v);
+            }
+            const int m = tid - kSConvWarp0 * 32;    // key row of the tile this thread rewrites
+#pragma unroll 1
+            for (int j = 0; j < n; ++j) {
+                const int s = j % kSStages, a = j & 1;
+                if (!mbar_wait(bar(SB_FULL + s), (j / kSStages) & 1, abort_flag, err)) break;
+                if (j >= 2 && !mbar_wait(bar(SB_AFREE + a), ((j >> 1) - 1) & 1, abort_flag, err)) break;
+                const uint8_t* stg = smem + SS_STG + s * kKeyTileBytes;
+                const uint2* src = reinterpret_cast<const uint2*>(stg + m * kIRow);
+                uint2 c[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) c[k] = src[k];
+                uint8_t* arow = smem + SS_A + a * 16384 + (m >> 3) * 1024 + (m & 7) * 128;
+#pragma unroll
+                for (int ch = 0; ch < 4; ++ch)
+                    *reinterpret_cast<uint4*>(arow + ((ch ^ (m & 7)) << 4)) =
+                        make_uint4(c[2 * ch].x, c[2 * ch].y, c[2 * ch + 1].x, c[2 * ch + 1].y);
+                // key scales of rows lane, 32 + lane, 64 + lane, 96 + lane into this sub-partition
+                uint32_t sv[8];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint2 w = *reinterpret_cast<const uint2*>(stg + (32 * q + lane) * kIRow + 64);
+                    sv[q] = w.x;
+                    sv[4 + q] = w.y;
+                }
+                tmem_st4(tmem + lane_base + kSTSFA + 8 * a, sv[0], sv[1], sv[2], sv[3]);
+                tmem_st4(tmem + lane_base + kSTSFA + 8 * a + 4, sv[4], sv[5], sv[6], sv[7]);
+                tmem_wait_st();
+                fence_proxy_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(bar(SB_FREE + s));
+                    mbar_arrive(bar(SB_AFULL + a));
+                }
             }
         }
-        __syncthreads();
-        if (tid < kITile) {
-            const float sum = red[tid] + red[kITile + tid];
-            const int pos = tile * kITile + tid;
-            if (pos < L) p.scores[static_cast<int64_t>(b) * p.tiles * kITile + pos] = tile_ok[tid] ? sum : -INFINITY;
+    } else {
+        warpgroup_reg_alloc<kSRegsEpi>();
+        if (warp < kSEpiWarp0 + 4) index_q_prep(p, b, smem, warp - kSConvWarp0, lane);
+        fence_proxy_async_smem();
+        named_bar_sync(kSPrepBar, 12 * 32);
+        const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+        {
+            // ======================================================== weighted head sums
+            const uint32_t wq = sbase + SS_WQ;      // read every tile (kept in registers, they spill)
+            float* out = p.scores + static_cast<int64_t>(b) * p.tiles * kITile;
+            const int a = (warp - kSEpiWarp0) >> 2;  // this set's accumulator: tiles j = a, a + 2, ...
+            const int my = 32 * (warp & 3) + lane;
+            // the table entry of this thread's position in tile jj (-1 past the visible end),
+            // loaded a tile of this set ahead and tested only where it is used, so the load's
+            // latency is hidden behind a whole tile
+            auto page_of = [&](int jj) -> int {
+                const int pos = (t0 + jj) * kITile + my;
+                return (jj < n && pos < L) ? __ldg(p.tables + b * p.tables_stride + (pos >> p.page_shift)) : -1;
+            };
+            int pg_cur = page_of(a);
+#pragma unroll 1
+            for (int j = a; j < n; j += 2) {
+                const int pg_next = page_of(j + 2);
+                if (!mbar_wait(bar(SB_DFULL + a), (j >> 1) & 1, abort_flag, err)) break;
+                tc_fence_after();
+                float acc = 0.0f;
+#pragma unroll 1
+                for (int hh = 0; hh < 4; ++hh) {   // unrolled, every TMEM load is hoisted and spills
+                    uint32_t lo[16], hi[16];
+                    tmem_ld16(tmem + lane_base + kSTD + 128 * a + 16 * hh, lo);
+                    tmem_ld16(tmem + lane_base + kSTD + 128 * a + 64 + 16 * hh, hi);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int h4 = 0; h4 < 4; ++h4) {
+                        const float4 w4 = lds_f32x4(wq + 64 * hh + 16 * h4);
+                        const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                        for (int h = 0; h < 4; ++h)
+                            acc = fmaf(wv[h], fmaxf(__uint_as_float(lo[4 * h4 + h]) + __uint_as_float(hi[4 * h4 + h]), 0.0f),
+                                       acc);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(SB_DFREE + a));
+                const int pos = (t0 + j) * kITile + my;
+                if (pos < L) out[pos] = (pg_cur >= 0 && pg_cur < p.num_pages) ? acc : -INFINITY;
+                pg_cur = pg_next;
+            }
         }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kSAllocWarp) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kSTCols);
     }
 }
 
@@ -478,12 +651,12 @@ extern "C" int nvfp4kv_index_topk(const void* q, int64_t q_stride_b, int64_t q_s
     if (num_heads != kIHeads) return fail(NVFP4KV_EINVAL, "index_topk: num_heads must be 64 (got %d)", num_heads);
     if (topk < 1 || max_seq_len < 0) return fail(NVFP4KV_EINVAL, "index_topk: bad topk / max_seq_len");
     if (pool_rows <= 0) return fail(NVFP4KV_EINVAL, "index_topk: empty index pool");
-    if (page_size <= 0 || (page_size & (page_size - 1)) || page_size > 4096 || pool_rows % page_size)
-        return fail(NVFP4KV_EINVAL, "index_topk: page_size must be a power of two <= 4096 dividing pool_rows");
+    if (page_size < 2 || (page_size & (page_size - 1)) || page_size > 4096 || pool_rows % page_size)
+        return fail(NVFP4KV_EINVAL, "index_topk: page_size must be a power of two in [2, 4096] dividing pool_rows");
     if (reinterpret_cast<uintptr_t>(q) % 16 || q_stride_b % 8 || q_stride_h % 8 ||
-        reinterpret_cast<uintptr_t>(index_pool) % 8)
+        reinterpret_cast<uintptr_t>(index_pool) % 16)
         return fail(NVFP4KV_EINVAL, "index_topk: q must be 16-byte aligned with strides multiples of 8, "
-                                    "the index pool 8-byte aligned");
+                                    "the index pool 16-byte aligned");
     size_t need = 0;
     nvfp4kv_index_topk_workspace_size(batch, max_seq_len, &need);
     if (need > 0 && (!workspace || workspace_bytes < need))
@@ -511,9 +684,17 @@ extern "C" int nvfp4kv_index_topk(const void* q, int64_t q_stride_b, int64_t q_s
         sp.tables = tables; sp.tables_stride = tables_stride; sp.seq_lens = seq_lens;
         sp.page_shift = shift; sp.max_seq_len = max_seq_len; sp.tiles = tiles;
         sp.scores = static_cast<float*>(workspace);
-        const int64_t runs = (tiles + kTilesPerBlock - 1) / kTilesPerBlock;
-        index_score_kernel<<<static_cast<unsigned>(static_cast<int64_t>(batch) * runs), 256, kScoreSmem, st>>>(
-            sp, err_flag);
+        // one wave: B entries x runs blocks on the SMs (one block per SM), at least one tile a run
+        static int sm_count[64] = {0};
+        int sms = dev >= 0 && dev < 64 ? sm_count[dev] : 0;
+        if (sms <= 0) {
+            if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+                return fail(NVFP4KV_ECUDA, "index_topk: SM count unavailable");
+            if (dev >= 0 && dev < 64) sm_count[dev] = sms;
+        }
+        sp.runs = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, sms / batch)));
+        index_score_kernel<<<static_cast<unsigned>(static_cast<int64_t>(batch) * sp.runs), kSThreads, kScoreSmem,
+                             st>>>(sp, err_flag);
         int rc = check_launch("nvfp4kv_index_topk (scores)");
         if (rc != NVFP4KV_OK) return rc;
     }
