@@ -79,45 +79,52 @@ __device__ __forceinline__ int64_t index_row(const int32_t* tables, int64_t stri
 // that its largest |q| lies in [2^10, 2^11)); 2^e_h goes into the head's weight, since
 // max(c x, 0) = c max(x, 0) for c > 0.
 //
-// Warps (512 threads): 0 loads (page runs of the pool, bulk copies into a ring of raw tiles;
-// the run's page ids staged in shared memory a window at a time, so no copy waits on a table
-// load), 1 issues the MMAs, 2 owns the TMEM allocation, 4-7 rewrite each raw tile into the
-// 128-byte swizzled operand layout and its scales into TMEM (warp w: sub-partition w & 3),
-// 8-15 read a finished tile's 128 accumulator columns (thread = key position) and write the
-// ReLU-weighted head sum: warps 8-11 the tiles of accumulator 0, 12-15 those of accumulator 1,
-// so each set has two tile periods per tile.  Warps 4-11 quantise q at the start.  Every wait
-// is bounded (common.cuh).
-constexpr int kSStages = 6;                                  // raw key tiles in flight
+// Every stage works on tiles of 128 keys, and each hand-off between stages costs about a memory
+// latency, so every stage runs as several copies over interleaved tiles (ring depth 3):
+// warps 0, 2, 3 load (tile j from loader j mod 3: page runs of the pool bulk-copied into a ring
+// of raw tiles, the run's page ids staged in shared memory a window at a time, so no copy waits
+// on a table load); warp 1 issues the MMAs; warps 4-7 rewrite each raw tile into the 128-byte
+// swizzled operand layout and its scales into TMEM (warp w: sub-partition w & 3); warps 8-19,
+// three sets of four, read a finished tile's 128 accumulator columns (thread = key position)
+// and write the ReLU-weighted head sum, set e taking the tiles j = e mod 3 in accumulator e.
+// Warps 4-11 quantise q at the start.  Warp 2 also owns the TMEM allocation.  Every wait is
+// bounded (common.cuh).
+constexpr int kSStages = 8;                                  // raw key tiles in flight
+constexpr int kSDepth = 3;                                   // operand buffers, accumulators, loaders, epilogue sets
 constexpr int kKeyTileBytes = kITile * kIRow;                // 9216
-constexpr int kSThreads = 512;
-constexpr int kSLoadWarp = 0, kSMmaWarp = 1, kSAllocWarp = 2, kSConvWarp0 = 4, kSEpiWarp0 = 8;
-constexpr int kSPrepBar = 1;                                 // named barrier of warps 4-15
-constexpr int kPgWin = 1024;                                 // page ids the loader stages at a time
-// Registers moved between warpgroups at run time (setmaxnreg; launched with 128 a thread): the
-// epilogue keeps the 64 head weights in registers.
-constexpr uint32_t kSRegsCtl = 64, kSRegsConv = 96, kSRegsEpi = 168;
-static_assert(128 * (kSRegsCtl + kSRegsConv + 2 * kSRegsEpi) <= kSThreads * 128, "register split within the launch");
+constexpr int kSThreads = 640;                               // 20 warps
+constexpr int kSMmaWarp = 1, kSAllocWarp = 2, kSConvWarp0 = 4, kSEpiWarp0 = 8;
+constexpr int kSPrepBar = 1;                                 // named barrier of warps 4-19
+constexpr int kSLoadBar = 2;                                 // named barrier of the three loaders
+constexpr int kPgWin = 512;                                  // page ids a loader stages at a time
+// Registers moved between warpgroups at run time (setmaxnreg).  The block is launched with
+// kSLaunchRegs a thread (ptxas's figure for 640 threads, one block per SM).
+constexpr uint32_t kSLaunchRegs = 96;
+constexpr uint32_t kSRegsCtl = 48, kSRegsConv = 72, kSRegsEpi = 120;
+static_assert(128 * (kSRegsCtl + kSRegsConv + kSDepth * kSRegsEpi) <= kSThreads * kSLaunchRegs,
+              "register split within the launch");
 constexpr int SS_QB = 0;                                     // Q terms: 2 passes x [128 rows x 128 B], 64 B used
-constexpr int SS_A = SS_QB + 2 * 16384;                      // 2 x key codes [128 rows x 128 B], 64 B used
-constexpr int SS_STG = SS_A + 2 * 16384;                     // kSStages x [128 rows x 72 B] as copied
+constexpr int SS_A = SS_QB + 2 * 16384;                      // kSDepth x key codes [128 rows x 128 B], 64 B used
+constexpr int SS_STG = SS_A + kSDepth * 16384;               // kSStages x [128 rows x 72 B] as copied
 constexpr int SS_QSF = SS_STG + kSStages * kKeyTileBytes;    // [2 passes][128 rows][8] Q-term scales
 constexpr int SS_WQ = SS_QSF + 2 * 128 * 8;                  // 64 f32: w[h] 2^e_h
-constexpr int SS_PG = SS_WQ + 256;                           // kPgWin i32: the loader's page ids
-constexpr int SS_FLAGS = SS_PG + kPgWin * 4;                 // [0] TMEM base, [1] abort
+constexpr int SS_PG = SS_WQ + 256;                           // kSDepth x kPgWin i32: each loader's page ids
+constexpr int SS_LAST = SS_PG + kSDepth * kPgWin * 4;        // kSDepth i32: each loader's last tile
+constexpr int SS_FLAGS = SS_LAST + 16;                       // [0] TMEM base, [1] abort
 constexpr int SS_BARS = SS_FLAGS + 16;
 constexpr int SB_FULL = 0;                                   // [stages] raw tile landed
 constexpr int SB_FREE = SB_FULL + kSStages;                  // [stages] converters done with it
-constexpr int SB_AFULL = SB_FREE + kSStages;                 // [2] operand tile + its scales ready
-constexpr int SB_AFREE = SB_AFULL + 2;                       // [2] MMAs done reading them
-constexpr int SB_DFULL = SB_AFREE + 2;                       // [2] accumulator complete
-constexpr int SB_DFREE = SB_DFULL + 2;                       // [2] accumulator read
-constexpr int SB_DRAIN = SB_DFREE + 2;                       // every MMA complete (before TMEM is freed)
+constexpr int SB_AFULL = SB_FREE + kSStages;                 // [depth] operand tile + its scales ready
+constexpr int SB_AFREE = SB_AFULL + kSDepth;                 // [depth] MMAs done reading them
+constexpr int SB_DFULL = SB_AFREE + kSDepth;                 // [depth] accumulator complete
+constexpr int SB_DFREE = SB_DFULL + kSDepth;                 // [depth] accumulator read
+constexpr int SB_DRAIN = SB_DFREE + kSDepth;                 // every MMA complete (before TMEM is freed)
 constexpr int kSBars = SB_DRAIN + 1;
 constexpr int kScoreSmem = SS_BARS + kSBars * 8 + 1024;      // slack to align the base
 static_assert(kScoreSmem <= 232448, "shared memory budget");
-constexpr uint32_t kSTD = 0;        // 2 x 128 columns: accumulators
-constexpr uint32_t kSTSFA = 256;    // 2 x 8 columns: key scales (column 4 kk + q: word kk of row 32 q + lane)
-constexpr uint32_t kSTSFB = 272;    // 16 columns: Q-term scales (8 pass + 4 kk + q)
+constexpr uint32_t kSTD = 0;        // kSDepth x 128 columns: accumulators
+constexpr uint32_t kSTSFA = 384;    // kSDepth x 8 columns: key scales (column 4 kk + q: word kk of row 32 q + lane)
+constexpr uint32_t kSTSFB = 416;    // 16 columns: Q-term scales (8 pass + 4 kk + q)
 constexpr uint32_t kSTCols = 512;
 static_assert(kIDim == 2 * 64 && kIRow == kIDim / 2 + kIDim / 16, "a key row: two K-chunks of 64 codes, then their scales");
 
@@ -207,7 +214,7 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
             mbar_init(bar(SB_FULL + s), 1);
             mbar_init(bar(SB_FREE + s), 4);
         }
-        for (int a = 0; a < 2; ++a) {
+        for (int a = 0; a < kSDepth; ++a) {
             mbar_init(bar(SB_AFULL + a), 4);
             mbar_init(bar(SB_AFREE + a), 1);
             mbar_init(bar(SB_DFULL + a), 1);
@@ -230,28 +237,30 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
     // allocates every role within its budget
     if (warp < kSConvWarp0) {
     warpgroup_reg_dealloc<kSRegsCtl>();
-    if (warp == kSLoadWarp) {
+    if (warp != kSMmaWarp) {
         // ============================================================ loads
-        // a tile is 128 / page runs of one page each (pages of <= 128 positions) or 128 rows
-        // of one page; runs of pages that are missing or lie wholly past the visible end are
-        // not copied (their positions score -inf or are not written)
+        // loader li takes tiles j = li mod kSDepth.  A tile is 128 / page runs of one page each
+        // (pages of <= 128 positions) or 128 rows of one page; runs of pages that are missing
+        // or lie wholly past the visible end are not copied (their positions score -inf or are
+        // not written).  A bulk copy that overwrites a stage the converters only read needs no
+        // proxy fence: their reads are ordered before it by the stage's barrier.
+        const int li = warp == 0 ? 0 : warp - 1;
         const int run_rows = p.page_shift >= 7 ? kITile : (1 << p.page_shift);
         const int runs_per_tile = kITile / run_rows;
         const uint32_t run_bytes = static_cast<uint32_t>(run_rows * kIRow);
-        int* pgw = reinterpret_cast<int*>(smem + SS_PG);   // page ids of pages wbase .. wbase + kPgWin - 1
+        int* pgw = reinterpret_cast<int*>(smem + SS_PG) + li * kPgWin;   // pages wbase .. wbase + kPgWin - 1
         const int last_page = (min(t1 * kITile, L) - 1) >> p.page_shift;
         int wbase = -2 * kPgWin;
-        int issued = 0;
+        int last = -1;                               // the last tile this loader issued
 #pragma unroll 1
-        for (int j = 0; j < n; ++j) {
+        for (int j = li; j < n; j += kSDepth) {
             const int s = j % kSStages;
             if (j >= kSStages) {
                 const bool ok = mbar_wait(bar(SB_FREE + s), ((j / kSStages) - 1) & 1, abort_flag, err);
                 if (!ok || *abort_flag) break;
-                fence_proxy_async_smem();
             }
             const int pos0 = (t0 + j) * kITile;
-            const int pfirst = pos0 >> p.page_shift, plast = min(pos0 + kITile, L) - 1 >> p.page_shift;
+            const int pfirst = pos0 >> p.page_shift, plast = (min(pos0 + kITile, L) - 1) >> p.page_shift;
             if (pfirst < wbase || plast >= wbase + kPgWin) {   // the tile's pages: one window (<= 64 pages)
                 __syncwarp();
                 wbase = pfirst;
@@ -259,44 +268,62 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
                 for (int k = lane; k < cnt; k += 32) pgw[k] = __ldg(p.tables + b * p.tables_stride + wbase + k);
                 __syncwarp();
             }
-            auto run_page = [&](int pos) -> int {   // page id of a visible position, -1 off the pool
-                const int pg = pgw[(pos >> p.page_shift) - wbase];
-                return (pg < 0 || pg >= p.num_pages) ? -1 : pg;
-            };
-            uint32_t bytes = 0;
-            for (int r = lane; r < runs_per_tile; r += 32) {
-                const int pos = pos0 + r * run_rows;
-                if (pos < L && run_page(pos) >= 0) bytes += run_bytes;
+            // runs r = lane, lane + 32 (at most 64 a tile): page id, or -1 (not copied)
+            int pg[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int r = lane + 32 * h, pos = pos0 + r * run_rows;
+                pg[h] = -1;
+                if (r < runs_per_tile && pos < L) {
+                    const int v = pgw[(pos >> p.page_shift) - wbase];
+                    pg[h] = (v < 0 || v >= p.num_pages) ? -1 : v;
+                }
             }
-            bytes = __reduce_add_sync(0xFFFFFFFFu, bytes);
-            if (lane == 0) mbar_arrive_expect_tx(bar(SB_FULL + s), bytes);
+            const uint32_t nrun = __popc(__ballot_sync(0xFFFFFFFFu, pg[0] >= 0)) +
+                                  __popc(__ballot_sync(0xFFFFFFFFu, pg[1] >= 0));
+            if (lane == 0) mbar_arrive_expect_tx(bar(SB_FULL + s), nrun * run_bytes);
             __syncwarp();
-            for (int r = lane; r < runs_per_tile; r += 32) {
-                const int pos = pos0 + r * run_rows;
-                if (pos >= L) continue;
-                const int pg = run_page(pos);
-                if (pg >= 0) {
-                    const int64_t row = (static_cast<int64_t>(pg) << p.page_shift) | (pos & ((1 << p.page_shift) - 1));
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                if (pg[h] >= 0) {
+                    const int r = lane + 32 * h, pos = pos0 + r * run_rows;
+                    const int64_t row = (static_cast<int64_t>(pg[h]) << p.page_shift) | (pos & ((1 << p.page_shift) - 1));
                     bulk_copy_g2s(sbase + SS_STG + s * kKeyTileBytes + r * run_bytes, p.pool + row * kIRow, run_bytes,
                                   bar(SB_FULL + s));
                 }
-            }
-            issued = j + 1;
+            last = j;
         }
-        // copies in flight land before the CTA can exit
-        for (int j = issued > kSStages ? issued - kSStages : 0; j < issued; ++j)
-            mbar_drain_wait(bar(SB_FULL + j % kSStages), (j / kSStages) & 1);
+        // Copies in flight land before the CTA can exit.  Only a stage's last issued tile can
+        // still be in flight (a stage is re-armed after its tile was consumed), and only its
+        // phase is certain not to have been passed by a later tile of another loader, so once
+        // every loader has stopped, lane s of loader 0 waits for stage s's last tile.
+        if (lane == 0) reinterpret_cast<volatile int*>(smem + SS_LAST)[li] = last;
+        named_bar_sync(kSLoadBar, kSDepth * 32);
+        if (li == 0 && lane < kSStages) {
+            int t = -1;
+#pragma unroll 1
+            for (int l = 0; l < kSDepth; ++l) {   // loader l's last tile on stage `lane`
+                const int lj = reinterpret_cast<volatile int*>(smem + SS_LAST)[l];
+#pragma unroll 1
+                for (int j = lj; j >= 0 && j > lj - kSDepth * kSStages; j -= kSDepth)
+                    if (j % kSStages == lane) {
+                        t = max(t, j);
+                        break;
+                    }
+            }
+            if (t >= 0) mbar_drain_wait(bar(SB_FULL + lane), (t / kSStages) & 1);
+        }
         __syncwarp();
-    } else if (warp == kSMmaWarp) {
+    } else {
         // ============================================================ MMA issue
         constexpr uint32_t idq = idesc_fp4_f32(kITile, 128);
         const uint64_t dq = smem_desc_sw128(sbase + SS_QB, 16, 1024);
         const uint64_t da = smem_desc_sw128(sbase + SS_A, 16, 1024);
 #pragma unroll 1
         for (int j = 0; j < n; ++j) {
-            const int a = j & 1;
-            if (!mbar_wait(bar(SB_AFULL + a), (j >> 1) & 1, abort_flag, err)) break;
-            if (j >= 2 && !mbar_wait(bar(SB_DFREE + a), ((j >> 1) - 1) & 1, abort_flag, err)) break;
+            const int a = j % kSDepth, u = j / kSDepth;
+            if (!mbar_wait(bar(SB_AFULL + a), u & 1, abort_flag, err)) break;
+            if (u > 0 && !mbar_wait(bar(SB_DFREE + a), (u - 1) & 1, abort_flag, err)) break;
             tc_fence_after();
             if (elect_one()) {
 #pragma unroll
@@ -320,107 +347,103 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
         warpgroup_reg_dealloc<kSRegsConv>();
         index_q_prep(p, b, smem, warp - kSConvWarp0, lane);
         fence_proxy_async_smem();                    // the Q terms are read by the tensor core
-        named_bar_sync(kSPrepBar, 12 * 32);
+        named_bar_sync(kSPrepBar, (kSThreads / 32 - kSConvWarp0) * 32);
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-        {
-            // ======================================================== operand tiles
-            {   // Q-term scales into this sub-partition: column 8 ps + 4 kk + q = word kk of row 32 q + lane
-                uint32_t v[16];
+        // ============================================================ operand tiles
+        {   // Q-term scales into this sub-partition: column 8 ps + 4 kk + q = word kk of row 32 q + lane
+            uint32_t v[16];
 #pragma unroll
-                for (int ps = 0; ps < 2; ++ps)
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const uint2 w = *reinterpret_cast<const uint2*>(smem + SS_QSF + (ps * 128 + 32 * q + lane) * 8);
-                        v[8 * ps + q] = w.x;
-                        v[8 * ps + 4 + q] = w.y;
-                    }
-                tmem_st16(tmem + lane_base + kSTSFB, v);
-            }
-            const int m = tid - kSConvWarp0 * 32;    // key row of the tile this thread rewrites
-#pragma unroll 1
-            for (int j = 0; j < n; ++j) {
-                const int s = j % kSStages, a = j & 1;
-                if (!mbar_wait(bar(SB_FULL + s), (j / kSStages) & 1, abort_flag, err)) break;
-                if (j >= 2 && !mbar_wait(bar(SB_AFREE + a), ((j >> 1) - 1) & 1, abort_flag, err)) break;
-                const uint8_t* stg = smem + SS_STG + s * kKeyTileBytes;
-                const uint2* src = reinterpret_cast<const uint2*>(stg + m * kIRow);
-                uint2 c[8];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) c[k] = src[k];
-                uint8_t* arow = smem + SS_A + a * 16384 + (m >> 3) * 1024 + (m & 7) * 128;
-#pragma unroll
-                for (int ch = 0; ch < 4; ++ch)
-                    *reinterpret_cast<uint4*>(arow + ((ch ^ (m & 7)) << 4)) =
-                        make_uint4(c[2 * ch].x, c[2 * ch].y, c[2 * ch + 1].x, c[2 * ch + 1].y);
-                // key scales of rows lane, 32 + lane, 64 + lane, 96 + lane into this sub-partition
-                uint32_t sv[8];
+            for (int ps = 0; ps < 2; ++ps)
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    const uint2 w = *reinterpret_cast<const uint2*>(stg + (32 * q + lane) * kIRow + 64);
-                    sv[q] = w.x;
-                    sv[4 + q] = w.y;
+                    const uint2 w = *reinterpret_cast<const uint2*>(smem + SS_QSF + (ps * 128 + 32 * q + lane) * 8);
+                    v[8 * ps + q] = w.x;
+                    v[8 * ps + 4 + q] = w.y;
                 }
-                tmem_st4(tmem + lane_base + kSTSFA + 8 * a, sv[0], sv[1], sv[2], sv[3]);
-                tmem_st4(tmem + lane_base + kSTSFA + 8 * a + 4, sv[4], sv[5], sv[6], sv[7]);
-                tmem_wait_st();
-                fence_proxy_async_smem();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(bar(SB_FREE + s));
-                    mbar_arrive(bar(SB_AFULL + a));
-                }
+            tmem_st16(tmem + lane_base + kSTSFB, v);
+        }
+        const int m = tid - kSConvWarp0 * 32;        // key row of the tile this thread rewrites
+#pragma unroll 1
+        for (int j = 0; j < n; ++j) {
+            const int s = j % kSStages, a = j % kSDepth, u = j / kSDepth;
+            if (!mbar_wait(bar(SB_FULL + s), (j / kSStages) & 1, abort_flag, err)) break;
+            if (u > 0 && !mbar_wait(bar(SB_AFREE + a), (u - 1) & 1, abort_flag, err)) break;
+            const uint8_t* stg = smem + SS_STG + s * kKeyTileBytes;
+            const uint2* src = reinterpret_cast<const uint2*>(stg + m * kIRow);
+            uint2 c[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) c[k] = src[k];
+            uint8_t* arow = smem + SS_A + a * 16384 + (m >> 3) * 1024 + (m & 7) * 128;
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch)
+                *reinterpret_cast<uint4*>(arow + ((ch ^ (m & 7)) << 4)) =
+                    make_uint4(c[2 * ch].x, c[2 * ch].y, c[2 * ch + 1].x, c[2 * ch + 1].y);
+            // key scales of rows lane, 32 + lane, 64 + lane, 96 + lane into this sub-partition
+            uint32_t sv[8];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint2 w = *reinterpret_cast<const uint2*>(stg + (32 * q + lane) * kIRow + 64);
+                sv[q] = w.x;
+                sv[4 + q] = w.y;
+            }
+            tmem_st4(tmem + lane_base + kSTSFA + 8 * a, sv[0], sv[1], sv[2], sv[3]);
+            tmem_st4(tmem + lane_base + kSTSFA + 8 * a + 4, sv[4], sv[5], sv[6], sv[7]);
+            tmem_wait_st();
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(bar(SB_FREE + s));
+                mbar_arrive(bar(SB_AFULL + a));
             }
         }
     } else {
         warpgroup_reg_alloc<kSRegsEpi>();
         if (warp < kSEpiWarp0 + 4) index_q_prep(p, b, smem, warp - kSConvWarp0, lane);
         fence_proxy_async_smem();
-        named_bar_sync(kSPrepBar, 12 * 32);
+        named_bar_sync(kSPrepBar, (kSThreads / 32 - kSConvWarp0) * 32);
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-        {
-            // ======================================================== weighted head sums
-            const uint32_t wq = sbase + SS_WQ;      // read every tile (kept in registers, they spill)
-            float* out = p.scores + static_cast<int64_t>(b) * p.tiles * kITile;
-            const int a = (warp - kSEpiWarp0) >> 2;  // this set's accumulator: tiles j = a, a + 2, ...
-            const int my = 32 * (warp & 3) + lane;
-            // the table entry of this thread's position in tile jj (-1 past the visible end),
-            // loaded a tile of this set ahead and tested only where it is used, so the load's
-            // latency is hidden behind a whole tile
-            auto page_of = [&](int jj) -> int {
-                const int pos = (t0 + jj) * kITile + my;
-                return (jj < n && pos < L) ? __ldg(p.tables + b * p.tables_stride + (pos >> p.page_shift)) : -1;
-            };
-            int pg_cur = page_of(a);
+        // ============================================================ weighted head sums
+        const uint32_t wq = sbase + SS_WQ;          // read every tile (kept in registers, they spill)
+        float* out = p.scores + static_cast<int64_t>(b) * p.tiles * kITile;
+        const int a = (warp - kSEpiWarp0) >> 2;      // this set's accumulator: tiles j = a mod kSDepth
+        const int my = 32 * (warp & 3) + lane;
+        // the table entry of this thread's position in tile jj (-1 past the visible end),
+        // loaded a tile of this set ahead and tested only where it is used, so the load's
+        // latency is hidden behind a whole tile
+        auto page_of = [&](int jj) -> int {
+            const int pos = (t0 + jj) * kITile + my;
+            return (jj < n && pos < L) ? __ldg(p.tables + b * p.tables_stride + (pos >> p.page_shift)) : -1;
+        };
+        int pg_cur = page_of(a);
 #pragma unroll 1
-            for (int j = a; j < n; j += 2) {
-                const int pg_next = page_of(j + 2);
-                if (!mbar_wait(bar(SB_DFULL + a), (j >> 1) & 1, abort_flag, err)) break;
-                tc_fence_after();
-                float acc = 0.0f;
+        for (int j = a; j < n; j += kSDepth) {
+            const int pg_next = page_of(j + kSDepth);
+            if (!mbar_wait(bar(SB_DFULL + a), (j / kSDepth) & 1, abort_flag, err)) break;
+            tc_fence_after();
+            float acc = 0.0f;
 #pragma unroll 1
-                for (int hh = 0; hh < 4; ++hh) {   // unrolled, every TMEM load is hoisted and spills
-                    uint32_t lo[16], hi[16];
-                    tmem_ld16(tmem + lane_base + kSTD + 128 * a + 16 * hh, lo);
-                    tmem_ld16(tmem + lane_base + kSTD + 128 * a + 64 + 16 * hh, hi);
-                    tmem_wait_ld();
+            for (int hh = 0; hh < 4; ++hh) {   // unrolled, every TMEM load is hoisted and spills
+                uint32_t lo[16], hi[16];
+                tmem_ld16(tmem + lane_base + kSTD + 128 * a + 16 * hh, lo);
+                tmem_ld16(tmem + lane_base + kSTD + 128 * a + 64 + 16 * hh, hi);
+                tmem_wait_ld();
 #pragma unroll
-                    for (int h4 = 0; h4 < 4; ++h4) {
-                        const float4 w4 = lds_f32x4(wq + 64 * hh + 16 * h4);
-                        const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+                for (int h4 = 0; h4 < 4; ++h4) {
+                    const float4 w4 = lds_f32x4(wq + 64 * hh + 16 * h4);
+                    const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-                        for (int h = 0; h < 4; ++h)
-                            acc = fmaf(wv[h], fmaxf(__uint_as_float(lo[4 * h4 + h]) + __uint_as_float(hi[4 * h4 + h]), 0.0f),
-                                       acc);
-                    }
+                    for (int h = 0; h < 4; ++h)
+                        acc = fmaf(wv[h], fmaxf(__uint_as_float(lo[4 * h4 + h]) + __uint_as_float(hi[4 * h4 + h]), 0.0f),
+                                   acc);
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar(SB_DFREE + a));
-                const int pos = (t0 + j) * kITile + my;
-                if (pos < L) out[pos] = (pg_cur >= 0 && pg_cur < p.num_pages) ? acc : -INFINITY;
-                pg_cur = pg_next;
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(SB_DFREE + a));
+            const int pos = (t0 + j) * kITile + my;
+            if (pos < L) out[pos] = (pg_cur >= 0 && pg_cur < p.num_pages) ? acc : -INFINITY;
+            pg_cur = pg_next;
         }
     }
     tc_fence_before();

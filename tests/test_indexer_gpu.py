@@ -139,3 +139,30 @@ def test_index_topk_feeds_the_sparse_decode(rt):
     assert np.allclose(o, ref, rtol=2e-2, atol=1e-2)
     assert np.linalg.norm(o - ref) / np.linalg.norm(ref) < 1e-2
     assert rt.device_errors() == 0
+
+
+def test_index_topk_long_runs_wrap_every_ring(rt):
+    """16 entries of 16K positions: each score block takes about 15 key tiles, so the key ring
+    and the operand, accumulator and loader rings all wrap several times.  The scores and the
+    selection are checked as above, and a call must end promptly: a ring that stalls shows up
+    as bounded waits running to their limit, not as an error."""
+    import time
+    lens = [16384] * 16
+    pages = 16 * 256
+    pool_np, tables, q, w, sl, rows, counts, gs, rs = _case(rt, lens, pages, seed=11)
+    for b, n in enumerate(lens):
+        ref, got = rs[b], gs[b, :n]
+        assert np.allclose(got, ref, rtol=1e-4, atol=1e-4 * np.abs(ref).max())
+        pos = O.index_select(got.astype(np.float64), 2048)
+        pg = tables[b].numpy()[pos // 64].astype(np.int64)
+        assert np.array_equal(rows[b, :len(pos)], pg * 64 + pos % 64)
+    pool = torch.from_numpy(pool_np).cuda().view(pages, 64, 72)
+    args = (q.cuda(), w.cuda(), pool, tables.cuda(), sl.cuda(), max(lens), 2048)
+    rt.index_topk(*args)
+    torch.cuda.synchronize()
+    t = time.perf_counter()
+    for _ in range(3):
+        rt.index_topk(*args)
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t < 0.3, "index_topk took seconds: a pipeline wait ran to its limit"
+    assert rt.device_errors() == 0
