@@ -81,35 +81,40 @@ __device__ __forceinline__ int64_t index_row(const int32_t* tables, int64_t stri
 //
 // Every stage works on tiles of 128 keys, and each hand-off between stages costs about a memory
 // latency, so every stage runs as several copies over interleaved tiles (ring depth 3):
-// warps 0, 2, 3 load (tile j from loader j mod 3: page runs of the pool bulk-copied into a ring
+// warps 0 and 2 load (tile j from loader j mod 2: page runs of the pool bulk-copied into a ring
 // of raw tiles, the run's page ids staged in shared memory a window at a time, so no copy waits
-// on a table load); warp 1 issues the MMAs; warps 4-7 rewrite each raw tile into the 128-byte
-// swizzled operand layout and its scales into TMEM (warp w: sub-partition w & 3); warps 8-19,
-// three sets of four, read a finished tile's 128 accumulator columns (thread = key position)
-// and write the ReLU-weighted head sum, set e taking the tiles j = e mod 3 in accumulator e.
-// Warps 4-11 quantise q at the start.  Warp 2 also owns the TMEM allocation.  Every wait is
-// bounded (common.cuh).
+// on a table load); warps 1 and 3 issue the MMAs of alternate tiles (an issuing thread stalls
+// until the tensor core takes its MMAs, so one warp's barrier waits overlap the other's issue);
+// warps 4-11, two sets of four taking alternate
+// tiles, rewrite each raw tile into the 128-byte swizzled operand layout and its scales into
+// TMEM (warp w: sub-partition w & 3); warps 12-23, three sets of four, read a finished tile's
+// 128 accumulator columns (thread = key position) and write the ReLU-weighted head sum, set e
+// taking the tiles j = e mod 3 in accumulator e.  Warps 4-11 quantise q at the start.  Warp 2
+// also owns the TMEM allocation.  Every wait is bounded (common.cuh).
 constexpr int kSStages = 8;                                  // raw key tiles in flight
-constexpr int kSDepth = 3;                                   // operand buffers, accumulators, loaders, epilogue sets
+constexpr int kSDepth = 3;                                   // operand buffers, accumulators, epilogue sets
+constexpr int kSLoaders = 2;                                 // warps 0, 2
+constexpr int kSMmaWarps = 2;                                // warps 1, 3
 constexpr int kKeyTileBytes = kITile * kIRow;                // 9216
-constexpr int kSThreads = 640;                               // 20 warps
-constexpr int kSMmaWarp = 1, kSAllocWarp = 2, kSConvWarp0 = 4, kSEpiWarp0 = 8;
-constexpr int kSPrepBar = 1;                                 // named barrier of warps 4-19
-constexpr int kSLoadBar = 2;                                 // named barrier of the three loaders
+constexpr int kSConvSets = 2;
+constexpr int kSThreads = 768;                               // 24 warps
+constexpr int kSAllocWarp = 2, kSConvWarp0 = 4, kSEpiWarp0 = 12;
+constexpr int kSPrepBar = 1;                                 // named barrier of warps 4-23
+constexpr int kSLoadBar = 2;                                 // named barrier of the loaders
 constexpr int kPgWin = 512;                                  // page ids a loader stages at a time
 // Registers moved between warpgroups at run time (setmaxnreg).  The block is launched with
-// kSLaunchRegs a thread (ptxas's figure for 640 threads, one block per SM).
-constexpr uint32_t kSLaunchRegs = 96;
-constexpr uint32_t kSRegsCtl = 48, kSRegsConv = 72, kSRegsEpi = 120;
-static_assert(128 * (kSRegsCtl + kSRegsConv + kSDepth * kSRegsEpi) <= kSThreads * kSLaunchRegs,
+// kSLaunchRegs a thread (ptxas's figure for 768 threads, one block per SM).
+constexpr uint32_t kSLaunchRegs = 80;
+constexpr uint32_t kSRegsCtl = 48, kSRegsConv = 56, kSRegsEpi = 104;
+static_assert(128 * (kSRegsCtl + kSConvSets * kSRegsConv + kSDepth * kSRegsEpi) <= kSThreads * kSLaunchRegs,
               "register split within the launch");
 constexpr int SS_QB = 0;                                     // Q terms: 2 passes x [128 rows x 128 B], 64 B used
 constexpr int SS_A = SS_QB + 2 * 16384;                      // kSDepth x key codes [128 rows x 128 B], 64 B used
 constexpr int SS_STG = SS_A + kSDepth * 16384;               // kSStages x [128 rows x 72 B] as copied
 constexpr int SS_QSF = SS_STG + kSStages * kKeyTileBytes;    // [2 passes][128 rows][8] Q-term scales
 constexpr int SS_WQ = SS_QSF + 2 * 128 * 8;                  // 64 f32: w[h] 2^e_h
-constexpr int SS_PG = SS_WQ + 256;                           // kSDepth x kPgWin i32: each loader's page ids
-constexpr int SS_LAST = SS_PG + kSDepth * kPgWin * 4;        // kSDepth i32: each loader's last tile
+constexpr int SS_PG = SS_WQ + 256;                           // kSLoaders x kPgWin i32: each loader's page ids
+constexpr int SS_LAST = SS_PG + kSLoaders * kPgWin * 4;      // kSLoaders i32: each loader's last tile
 constexpr int SS_FLAGS = SS_LAST + 16;                       // [0] TMEM base, [1] abort
 constexpr int SS_BARS = SS_FLAGS + 16;
 constexpr int SB_FULL = 0;                                   // [stages] raw tile landed
@@ -119,7 +124,8 @@ constexpr int SB_AFREE = SB_AFULL + kSDepth;                 // [depth] MMAs don
 constexpr int SB_DFULL = SB_AFREE + kSDepth;                 // [depth] accumulator complete
 constexpr int SB_DFREE = SB_DFULL + kSDepth;                 // [depth] accumulator read
 constexpr int SB_DRAIN = SB_DFREE + kSDepth;                 // every MMA complete (before TMEM is freed)
-constexpr int kSBars = SB_DRAIN + 1;
+constexpr int SB_QREADY = SB_DRAIN + 1;                      // Q-term scales in TMEM (every sub-partition)
+constexpr int kSBars = SB_QREADY + 1;
 constexpr int kScoreSmem = SS_BARS + kSBars * 8 + 1024;      // slack to align the base
 static_assert(kScoreSmem <= 232448, "shared memory budget");
 constexpr uint32_t kSTD = 0;        // kSDepth x 128 columns: accumulators
@@ -127,6 +133,26 @@ constexpr uint32_t kSTSFA = 384;    // kSDepth x 8 columns: key scales (column 4
 constexpr uint32_t kSTSFB = 416;    // 16 columns: Q-term scales (8 pass + 4 kk + q)
 constexpr uint32_t kSTCols = 512;
 static_assert(kIDim == 2 * 64 && kIRow == kIDim / 2 + kIDim / 16, "a key row: two K-chunks of 64 codes, then their scales");
+
+// Packed pairs of fp32 (sm_100 f32x2 arithmetic: one instruction for two lanes of work).
+__device__ __forceinline__ uint64_t pack_f32x2(uint32_t lo, uint32_t hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpack_f32x2(uint64_t v, uint32_t& lo, uint32_t& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
 
 // Four floats from shared memory, issued where written (not hoisted out of a loop).
 __device__ __forceinline__ float4 lds_f32x4(uint32_t addr) {
@@ -220,7 +246,8 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
             mbar_init(bar(SB_DFULL + a), 1);
             mbar_init(bar(SB_DFREE + a), 4);
         }
-        mbar_init(bar(SB_DRAIN), 1);
+        mbar_init(bar(SB_DRAIN), kSMmaWarps);
+        mbar_init(bar(SB_QREADY), 4);
         flags[1] = 0;
         mbar_fence_init();
     }
@@ -237,14 +264,14 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
     // allocates every role within its budget
     if (warp < kSConvWarp0) {
     warpgroup_reg_dealloc<kSRegsCtl>();
-    if (warp != kSMmaWarp) {
+    if ((warp & 1) == 0) {
         // ============================================================ loads
-        // loader li takes tiles j = li mod kSDepth.  A tile is 128 / page runs of one page each
+        // loader li takes tiles j = li mod kSLoaders.  A tile is 128 / page runs of one page each
         // (pages of <= 128 positions) or 128 rows of one page; runs of pages that are missing
         // or lie wholly past the visible end are not copied (their positions score -inf or are
         // not written).  A bulk copy that overwrites a stage the converters only read needs no
         // proxy fence: their reads are ordered before it by the stage's barrier.
-        const int li = warp == 0 ? 0 : warp - 1;
+        const int li = warp >> 1;
         const int run_rows = p.page_shift >= 7 ? kITile : (1 << p.page_shift);
         const int runs_per_tile = kITile / run_rows;
         const uint32_t run_bytes = static_cast<uint32_t>(run_rows * kIRow);
@@ -253,7 +280,7 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
         int wbase = -2 * kPgWin;
         int last = -1;                               // the last tile this loader issued
 #pragma unroll 1
-        for (int j = li; j < n; j += kSDepth) {
+        for (int j = li; j < n; j += kSLoaders) {
             const int s = j % kSStages;
             if (j >= kSStages) {
                 const bool ok = mbar_wait(bar(SB_FREE + s), ((j / kSStages) - 1) & 1, abort_flag, err);
@@ -298,14 +325,14 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
         // phase is certain not to have been passed by a later tile of another loader, so once
         // every loader has stopped, lane s of loader 0 waits for stage s's last tile.
         if (lane == 0) reinterpret_cast<volatile int*>(smem + SS_LAST)[li] = last;
-        named_bar_sync(kSLoadBar, kSDepth * 32);
+        named_bar_sync(kSLoadBar, kSLoaders * 32);
         if (li == 0 && lane < kSStages) {
             int t = -1;
 #pragma unroll 1
-            for (int l = 0; l < kSDepth; ++l) {   // loader l's last tile on stage `lane`
+            for (int l = 0; l < kSLoaders; ++l) {   // loader l's last tile on stage `lane`
                 const int lj = reinterpret_cast<volatile int*>(smem + SS_LAST)[l];
 #pragma unroll 1
-                for (int j = lj; j >= 0 && j > lj - kSDepth * kSStages; j -= kSDepth)
+                for (int j = lj; j >= 0 && j > lj - kSLoaders * kSStages; j -= kSLoaders)
                     if (j % kSStages == lane) {
                         t = max(t, j);
                         break;
@@ -319,8 +346,12 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
         constexpr uint32_t idq = idesc_fp4_f32(kITile, 128);
         const uint64_t dq = smem_desc_sw128(sbase + SS_QB, 16, 1024);
         const uint64_t da = smem_desc_sw128(sbase + SS_A, 16, 1024);
+        // the Q-term scales are written by the first converter set only; a tile of the second
+        // set does not order them, so every MMA waits for them once
+        const bool qready = mbar_wait(bar(SB_QREADY), 0, abort_flag, err);
+        tc_fence_after();
 #pragma unroll 1
-        for (int j = 0; j < n; ++j) {
+        for (int j = warp >> 1; qready && j < n; j += kSMmaWarps) {   // this warp's tiles
             const int a = j % kSDepth, u = j / kSDepth;
             if (!mbar_wait(bar(SB_AFULL + a), u & 1, abort_flag, err)) break;
             if (u > 0 && !mbar_wait(bar(SB_DFREE + a), (u - 1) & 1, abort_flag, err)) break;
@@ -338,19 +369,20 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
             }
             __syncwarp();
         }
-        // every MMA of this CTA completes before its TMEM is freed, on the abort path too
+        // every MMA of this CTA (both issuing warps') completes before its TMEM is freed, on the
+        // abort path too
         if (elect_one()) tc_commit(bar(SB_DRAIN));
         __syncwarp();
         mbar_drain_wait(bar(SB_DRAIN), 0);
     }
     } else if (warp < kSEpiWarp0) {
         warpgroup_reg_dealloc<kSRegsConv>();
-        index_q_prep(p, b, smem, warp - kSConvWarp0, lane);
+        index_q_prep(p, b, smem, warp - kSConvWarp0, lane);   // both converter sets: warps 4-11
         fence_proxy_async_smem();                    // the Q terms are read by the tensor core
         named_bar_sync(kSPrepBar, (kSThreads / 32 - kSConvWarp0) * 32);
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
         // ============================================================ operand tiles
-        {   // Q-term scales into this sub-partition: column 8 ps + 4 kk + q = word kk of row 32 q + lane
+        if (warp < kSConvWarp0 + 4) {   // Q-term scales into this sub-partition: column 8 ps + 4 kk + q = word kk of row 32 q + lane
             uint32_t v[16];
 #pragma unroll
             for (int ps = 0; ps < 2; ++ps)
@@ -361,10 +393,15 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
                     v[8 * ps + 4 + q] = w.y;
                 }
             tmem_st16(tmem + lane_base + kSTSFB, v);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(SB_QREADY));
         }
-        const int m = tid - kSConvWarp0 * 32;        // key row of the tile this thread rewrites
+        const int m = (tid - kSConvWarp0 * 32) & (kITile - 1);   // key row of the tile this thread rewrites
+        const int cset = (warp - kSConvWarp0) >> 2;               // tiles j = cset mod kSConvSets
 #pragma unroll 1
-        for (int j = 0; j < n; ++j) {
+        for (int j = cset; j < n; j += kSConvSets) {
             const int s = j % kSStages, a = j % kSDepth, u = j / kSDepth;
             if (!mbar_wait(bar(SB_FULL + s), (j / kSStages) & 1, abort_flag, err)) break;
             if (u > 0 && !mbar_wait(bar(SB_AFREE + a), (u - 1) & 1, abort_flag, err)) break;
@@ -399,8 +436,6 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
         }
     } else {
         warpgroup_reg_alloc<kSRegsEpi>();
-        if (warp < kSEpiWarp0 + 4) index_q_prep(p, b, smem, warp - kSConvWarp0, lane);
-        fence_proxy_async_smem();
         named_bar_sync(kSPrepBar, (kSThreads / 32 - kSConvWarp0) * 32);
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
         // ============================================================ weighted head sums
@@ -421,28 +456,53 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
             const int pg_next = page_of(j + kSDepth);
             if (!mbar_wait(bar(SB_DFULL + a), (j / kSDepth) & 1, abort_flag, err)) break;
             tc_fence_after();
-            float acc = 0.0f;
-#pragma unroll 1
-            for (int hh = 0; hh < 4; ++hh) {   // unrolled, every TMEM load is hoisted and spills
-                uint32_t lo[16], hi[16];
-                tmem_ld16(tmem + lane_base + kSTD + 128 * a + 16 * hh, lo);
-                tmem_ld16(tmem + lane_base + kSTD + 128 * a + 64 + 16 * hh, hi);
-                tmem_wait_ld();
+            // heads 16 r .. 16 r + 15 in round r: columns 16 r + h (terms 1 + 3) and 64 + 16 r + h
+            // (terms 2 + 4); round r + 1's loads are issued before round r is summed
+            const uint32_t dcol = tmem + lane_base + kSTD + 128 * a;
+            uint64_t acc2[2] = {0ull, 0ull};   // two f32x2 accumulators
+            uint32_t lo0[16], hi0[16], lo1[16], hi1[16];
+            auto sum16 = [&](const uint32_t (&lo)[16], const uint32_t (&hi)[16], int r) {
 #pragma unroll
                 for (int h4 = 0; h4 < 4; ++h4) {
-                    const float4 w4 = lds_f32x4(wq + 64 * hh + 16 * h4);
-                    const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+                    const float4 w4 = lds_f32x4(wq + 64 * r + 16 * h4);
 #pragma unroll
-                    for (int h = 0; h < 4; ++h)
-                        acc = fmaf(wv[h], fmaxf(__uint_as_float(lo[4 * h4 + h]) + __uint_as_float(hi[4 * h4 + h]), 0.0f),
-                                   acc);
+                    for (int hp = 0; hp < 2; ++hp) {
+                        const int h = 4 * h4 + 2 * hp;
+                        uint64_t s2 = add_f32x2(pack_f32x2(lo[h], lo[h + 1]), pack_f32x2(hi[h], hi[h + 1]));
+                        uint32_t s0, s1;
+                        unpack_f32x2(s2, s0, s1);
+                        s2 = pack_f32x2(__float_as_uint(fmaxf(__uint_as_float(s0), 0.0f)),
+                                        __float_as_uint(fmaxf(__uint_as_float(s1), 0.0f)));
+                        const uint64_t w2 = hp ? pack_f32x2(__float_as_uint(w4.z), __float_as_uint(w4.w))
+                                               : pack_f32x2(__float_as_uint(w4.x), __float_as_uint(w4.y));
+                        acc2[hp] = fma_f32x2(w2, s2, acc2[hp]);
+                    }
                 }
+            };
+            tmem_ld16(dcol, lo0);
+            tmem_ld16(dcol + 64, hi0);
+#pragma unroll 1
+            for (int rp = 0; rp < 4; rp += 2) {
+                tmem_wait_ld();
+                tmem_ld16(dcol + 16 * (rp + 1), lo1);
+                tmem_ld16(dcol + 64 + 16 * (rp + 1), hi1);
+                sum16(lo0, hi0, rp);
+                tmem_wait_ld();
+                if (rp == 0) {
+                    tmem_ld16(dcol + 32, lo0);
+                    tmem_ld16(dcol + 96, hi0);
+                }
+                sum16(lo1, hi1, rp + 1);
             }
+            uint32_t a0, a1, a2, a3;
+            unpack_f32x2(acc2[0], a0, a1);
+            unpack_f32x2(acc2[1], a2, a3);
+            const float tot = (__uint_as_float(a0) + __uint_as_float(a2)) + (__uint_as_float(a1) + __uint_as_float(a3));
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(SB_DFREE + a));
             const int pos = (t0 + j) * kITile + my;
-            if (pos < L) out[pos] = (pg_cur >= 0 && pg_cur < p.num_pages) ? acc : -INFINITY;
+            if (pos < L) out[pos] = (pg_cur >= 0 && pg_cur < p.num_pages) ? tot : -INFINITY;
             pg_cur = pg_next;
         }
     }
