@@ -1455,6 +1455,30 @@ def host_link_gbs(torch, dev, h2d_step: int, d2h_step: int) -> dict:
         b.synchronize()
         us = a.elapsed_time(b) / 10 * 1e3
         res[name] = {"bytes": n, "us": round(us, 2), "GBs": round(n / us / 1e3, 1)}
+    # a step's input and output copies at the same time, on two streams (what an engine's
+    # pipelined step does): whether the link carries both directions at once
+    hi = torch.empty(h2d_step, dtype=torch.uint8).pin_memory()
+    di = torch.empty(h2d_step, dtype=torch.uint8, device=dev)
+    do = torch.empty(d2h_step, dtype=torch.uint8, device=dev)
+    ho = torch.empty(d2h_step, dtype=torch.uint8).pin_memory()
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    s1.wait_stream(torch.cuda.current_stream())
+    s2.wait_stream(torch.cuda.current_stream())
+    for _ in range(10):
+        with torch.cuda.stream(s1):
+            di.copy_(hi, non_blocking=True)
+        with torch.cuda.stream(s2):
+            ho.copy_(do, non_blocking=True)
+    torch.cuda.current_stream().wait_stream(s1)
+    torch.cuda.current_stream().wait_stream(s2)
+    b.record()
+    b.synchronize()
+    us = a.elapsed_time(b) / 10 * 1e3
+    res["both_step"] = {"bytes": h2d_step + d2h_step, "us": round(us, 2),
+                        "GBs": round((h2d_step + d2h_step) / us / 1e3, 1)}
     return res
 
 
