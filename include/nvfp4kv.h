@@ -290,7 +290,10 @@ int nvfp4kv_index_append(const void* k, int64_t num_tokens, int64_t src_stride, 
  * a position on a missing page: exactly the sparse tables and seq_lens nvfp4kv_mla_decode takes.
  * q: bf16 [batch, 64 heads, 128] with element strides (q_stride_b, q_stride_h), 16-byte
  * aligned; weights fp32 [batch, 64], row stride weights_stride; workspace: the scores,
- * nvfp4kv_index_topk_workspace_size() bytes, 16-byte aligned.
+ * nvfp4kv_index_topk_workspace_size() bytes, 16-byte aligned.  index_pool 16-byte aligned and
+ * page_size a power of two in [2, 4096] dividing pool_rows: the scoring kernel copies whole
+ * pages (or 128-row runs of them) with 16-byte bulk copies, and two 72-byte rows are the
+ * smallest run that is a multiple of 16 bytes.
  */
 int nvfp4kv_index_topk(const void* q, int64_t q_stride_b, int64_t q_stride_h, const float* weights,
                        int64_t weights_stride, const uint8_t* index_pool, int64_t pool_rows,

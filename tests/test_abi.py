@@ -195,3 +195,27 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "LIB_PATH", str(tmp_path / "absent.so"))
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         _lib.lib()
+
+
+def test_index_topk_argument_checks_without_launch():
+    """The page-copy contract of the scoring kernel (pages of at least two 72-byte rows, a
+    16-byte aligned pool) and the other argument checks fail before any launch."""
+    lib = _lib.lib()
+
+    def call(pool=4096, rows=4096, page=64, heads=64, ws=None, wsb=0, batch=2, q=4096):
+        # (q, q_sb, q_sh, w, w_sb, pool, pool_rows, tables, t_stride, seq_lens, batch, heads, page,
+        #  max_seq_len, topk, out_rows, out_count, ws, ws_bytes, err, stream)
+        return lib.nvfp4kv_index_topk(q, 64 * 128, 128, 4096, 64, pool, rows, 4096, 16, 4096, batch, heads, page,
+                                      1024, 2048, 4096, 4096, ws, wsb, None, None)
+    assert call(batch=0) == _lib.OK
+    assert call(q=None) == _lib.EINVAL
+    assert call(heads=32) == _lib.EINVAL
+    assert call(page=1) == _lib.EINVAL                   # a one-row page is not a 16-byte run
+    assert call(page=48) == _lib.EINVAL                  # not a power of two
+    assert call(rows=4000) == _lib.EINVAL                # pages do not divide the pool
+    assert call(pool=4104) == _lib.EINVAL                # pool not 16-byte aligned
+    assert call() == _lib.EWORKSPACE
+    need = ctypes.c_size_t()
+    assert lib.nvfp4kv_index_topk_workspace_size(2, 1024, ctypes.byref(need)) == _lib.OK
+    assert need.value == 2 * 1024 * 4
+    assert call(ws=4100, wsb=need.value) == _lib.EINVAL  # workspace not 16-byte aligned
