@@ -170,3 +170,39 @@ def test_index_topk_long_runs_wrap_every_ring(rt):
         rt.index_topk(*args)
     torch.cuda.synchronize()
     assert rt.device_errors() == 0
+
+
+@pytest.mark.parametrize("page", [2, 16, 256])
+def test_index_topk_other_page_sizes(rt, page):
+    """The scoring kernel copies a tile of 128 keys as 128 / page whole pages (2 and 16 rows) or
+    as a 128-row run inside one page (256 rows); sequence ends fall inside a tile and inside a
+    page, and one page is missing."""
+    lens = [3001, 777, 1500]
+    pages = (4096 + page - 1) // page * 2
+    pool_np = O.index_quant(_keys(pages * page, seed=page))
+    pool = torch.from_numpy(pool_np).cuda().view(pages, page, 72)
+    g = torch.Generator().manual_seed(page + 1)
+    width = (max(lens) + page - 1) // page
+    tables = torch.stack([torch.randperm(pages, generator=g)[:width] for _ in lens]).to(torch.int32)
+    tables[0, width // 2] = pages + 5                                   # a page outside the pool
+    q = torch.randn(len(lens), 64, 128, generator=g).to(torch.bfloat16)
+    w = torch.rand(len(lens), 64, generator=g) * 0.1
+    topk = 512
+    rows, counts = rt.index_topk(q.cuda(), w.cuda(), pool, tables.cuda(), torch.tensor(lens, dtype=torch.int32).cuda(),
+                                 max(lens), topk)
+    torch.cuda.synchronize()
+    ld = (max(lens) + 127) // 128 * 128
+    gs = rt.index_scores_buffer()[:len(lens) * ld].view(len(lens), ld).cpu().numpy()
+    rs = O.index_scores(q.float(), w, pool_np, tables.numpy(), lens, page_size=page)
+    rows, counts = rows.cpu().numpy(), counts.cpu().numpy()
+    for b, n in enumerate(lens):
+        ref, got = rs[b], gs[b, :n]
+        fin = np.isfinite(ref)
+        assert np.array_equal(np.isfinite(got), fin)
+        assert np.allclose(got[fin], ref[fin], rtol=1e-4, atol=1e-4 * np.abs(ref[fin]).max())
+        assert counts[b] == min(n, topk)
+        pos = O.index_select(got.astype(np.float64), topk)
+        pg = tables[b].numpy()[pos // page].astype(np.int64)
+        want = np.where((pg >= 0) & (pg < pages), pg * page + pos % page, -1)
+        assert np.array_equal(rows[b, :len(pos)], want), f"page {page}, entry {b}: selection differs"
+    assert rt.device_errors() == 0
