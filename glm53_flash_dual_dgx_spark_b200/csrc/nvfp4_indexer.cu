@@ -80,33 +80,36 @@ __device__ __forceinline__ int64_t index_row(const int32_t* tables, int64_t stri
 // max(c x, 0) = c max(x, 0) for c > 0.
 //
 // Every stage works on tiles of 128 keys, and each hand-off between stages costs about a memory
-// latency, so every stage runs as several copies over interleaved tiles (ring depth 3):
-// warps 0 and 2 load (tile j from loader j mod 2: page runs of the pool bulk-copied into a ring
-// of raw tiles, the run's page ids staged in shared memory a window at a time, so no copy waits
-// on a table load); warps 1 and 3 issue the MMAs of alternate tiles (an issuing thread stalls
-// until the tensor core takes its MMAs, so one warp's barrier waits overlap the other's issue);
-// warps 4-11, two sets of four taking alternate
-// tiles, rewrite each raw tile into the 128-byte swizzled operand layout and its scales into
-// TMEM (warp w: sub-partition w & 3); warps 12-23, three sets of four, read a finished tile's
-// 128 accumulator columns (thread = key position) and write the ReLU-weighted head sum, set e
-// taking the tiles j = e mod 3 in accumulator e.  Warps 4-11 quantise q at the start.  Warp 2
-// also owns the TMEM allocation.  Every wait is bounded (common.cuh).
-constexpr int kSStages = 8;                                  // raw key tiles in flight
+// latency, so the stages run as several copies over interleaved tiles: warps 0, 2 and 3 load
+// (tile j from loader j mod 3: page runs of the pool bulk-copied into a ring of raw tiles, the run's
+// page ids staged in shared memory a window at a time, so no copy waits on a table load);
+// warp 1 issues the MMAs; warps 4-7 rewrite each raw tile into the 128-byte swizzled operand
+// layout and its scales into TMEM (warp w: sub-partition w & 3), three operand buffers; warps
+// 8-19, three sets of four, read a finished tile's 128 accumulator columns (thread = key
+// position) and write the ReLU-weighted head sum, set e taking the tiles j = e mod 3 in
+// accumulator e.  Warps 4-7 quantise q at the start.  Warp 2 also owns the TMEM allocation.
+// Every wait is bounded (common.cuh).
+//
+// Every slot of every ring is waited on by one warp (or one set of warps) only, in phase order:
+// a parity wait cannot tell phase u - 1 from phase u + 1, so a second consumer of a slot that
+// reached its wait one phase early would pass at once.  Hence the ring depths: the 9 key
+// stages split over 3 loaders (stage s always loader s mod 3), 3 operand buffers and 3
+// accumulators each served by the one converter set, the one MMA warp and epilogue set e.
+constexpr int kSStages = 9;                                  // raw key tiles in flight
 constexpr int kSDepth = 3;                                   // operand buffers, accumulators, epilogue sets
-constexpr int kSLoaders = 2;                                 // warps 0, 2
-constexpr int kSMmaWarps = 2;                                // warps 1, 3
+constexpr int kSLoaders = 3;                                 // warps 0, 2, 3
+static_assert(kSStages % kSLoaders == 0, "a stage is always refilled by the same loader");
 constexpr int kKeyTileBytes = kITile * kIRow;                // 9216
-constexpr int kSConvSets = 2;
-constexpr int kSThreads = 768;                               // 24 warps
-constexpr int kSAllocWarp = 2, kSConvWarp0 = 4, kSEpiWarp0 = 12;
-constexpr int kSPrepBar = 1;                                 // named barrier of warps 4-23
+constexpr int kSThreads = 640;                               // 20 warps
+constexpr int kSMmaWarp = 1, kSAllocWarp = 2, kSConvWarp0 = 4, kSEpiWarp0 = 8;
+constexpr int kSPrepBar = 1;                                 // named barrier of warps 4-19
 constexpr int kSLoadBar = 2;                                 // named barrier of the loaders
 constexpr int kPgWin = 512;                                  // page ids a loader stages at a time
 // Registers moved between warpgroups at run time (setmaxnreg).  The block is launched with
-// kSLaunchRegs a thread (ptxas's figure for 768 threads, one block per SM).
-constexpr uint32_t kSLaunchRegs = 80;
-constexpr uint32_t kSRegsCtl = 48, kSRegsConv = 56, kSRegsEpi = 104;
-static_assert(128 * (kSRegsCtl + kSConvSets * kSRegsConv + kSDepth * kSRegsEpi) <= kSThreads * kSLaunchRegs,
+// kSLaunchRegs a thread (ptxas's figure for 640 threads, one block per SM).
+constexpr uint32_t kSLaunchRegs = 96;
+constexpr uint32_t kSRegsCtl = 80, kSRegsConv = 72, kSRegsEpi = 96;
+static_assert(128 * (kSRegsCtl + kSRegsConv + kSDepth * kSRegsEpi) <= kSThreads * kSLaunchRegs,
               "register split within the launch");
 constexpr int SS_QB = 0;                                     // Q terms: 2 passes x [128 rows x 128 B], 64 B used
 constexpr int SS_A = SS_QB + 2 * 16384;                      // kSDepth x key codes [128 rows x 128 B], 64 B used
@@ -163,13 +166,13 @@ __device__ __forceinline__ float4 lds_f32x4(uint32_t addr) {
 
 // q of entry b -> four NVFP4 terms in the B-operand image (term tt: pass tt >> 1, row
 // 64 (tt & 1) + h, K-major, 128-byte swizzle), their scales [pass][row][8], and w[h] 2^e_h.
-// Warps 4-11, eight lanes per head (lane j: dims 16 j .. 16 j + 15), four heads per warp and
-// round.
+// The four converter warps (wi = 0..3), eight lanes per head (lane j: dims 16 j .. 16 j + 15),
+// four heads per warp and round.
 __device__ __forceinline__ void index_q_prep(const ScoreParams& p, int b, uint8_t* smem, int wi, int lane) {
     const int j = lane & 7;
 #pragma unroll 1
-    for (int it = 0; it < 2; ++it) {
-        const int h = 32 * it + 4 * wi + (lane >> 3);
+    for (int it = 0; it < 4; ++it) {
+        const int h = 16 * it + 4 * wi + (lane >> 3);
         const __nv_bfloat16* src = p.q + b * p.q_sb + h * p.q_sh + 16 * j;
         const uint4 u0 = ldg_nc_v4(src), u1 = ldg_nc_v4(src + 8);
         const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
@@ -246,7 +249,7 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
             mbar_init(bar(SB_DFULL + a), 1);
             mbar_init(bar(SB_DFREE + a), 4);
         }
-        mbar_init(bar(SB_DRAIN), kSMmaWarps);
+        mbar_init(bar(SB_DRAIN), 1);
         mbar_init(bar(SB_QREADY), 4);
         flags[1] = 0;
         mbar_fence_init();
@@ -264,14 +267,14 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
     // allocates every role within its budget
     if (warp < kSConvWarp0) {
     warpgroup_reg_dealloc<kSRegsCtl>();
-    if ((warp & 1) == 0) {
+    if (warp != kSMmaWarp) {
         // ============================================================ loads
         // loader li takes tiles j = li mod kSLoaders.  A tile is 128 / page runs of one page each
         // (pages of <= 128 positions) or 128 rows of one page; runs of pages that are missing
         // or lie wholly past the visible end are not copied (their positions score -inf or are
         // not written).  A bulk copy that overwrites a stage the converters only read needs no
         // proxy fence: their reads are ordered before it by the stage's barrier.
-        const int li = warp >> 1;
+        const int li = warp == 0 ? 0 : warp - 1;
         const int run_rows = p.page_shift >= 7 ? kITile : (1 << p.page_shift);
         const int runs_per_tile = kITile / run_rows;
         const uint32_t run_bytes = static_cast<uint32_t>(run_rows * kIRow);
@@ -341,17 +344,16 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
             if (t >= 0) mbar_drain_wait(bar(SB_FULL + lane), (t / kSStages) & 1);
         }
         __syncwarp();
-    } else {
+    } else if (warp == kSMmaWarp) {
         // ============================================================ MMA issue
         constexpr uint32_t idq = idesc_fp4_f32(kITile, 128);
         const uint64_t dq = smem_desc_sw128(sbase + SS_QB, 16, 1024);
         const uint64_t da = smem_desc_sw128(sbase + SS_A, 16, 1024);
-        // the Q-term scales are written by the first converter set only; a tile of the second
-        // set does not order them, so every MMA waits for them once
+        // the Q-term scales in TMEM, written by the converter warps before their first tile
         const bool qready = mbar_wait(bar(SB_QREADY), 0, abort_flag, err);
         tc_fence_after();
 #pragma unroll 1
-        for (int j = warp >> 1; qready && j < n; j += kSMmaWarps) {   // this warp's tiles
+        for (int j = 0; qready && j < n; ++j) {
             const int a = j % kSDepth, u = j / kSDepth;
             if (!mbar_wait(bar(SB_AFULL + a), u & 1, abort_flag, err)) break;
             if (u > 0 && !mbar_wait(bar(SB_DFREE + a), (u - 1) & 1, abort_flag, err)) break;
@@ -369,20 +371,19 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
             }
             __syncwarp();
         }
-        // every MMA of this CTA (both issuing warps') completes before its TMEM is freed, on the
-        // abort path too
+        // every MMA of this CTA completes before its TMEM is freed, on the abort path too
         if (elect_one()) tc_commit(bar(SB_DRAIN));
         __syncwarp();
         mbar_drain_wait(bar(SB_DRAIN), 0);
     }
     } else if (warp < kSEpiWarp0) {
         warpgroup_reg_dealloc<kSRegsConv>();
-        index_q_prep(p, b, smem, warp - kSConvWarp0, lane);   // both converter sets: warps 4-11
+        index_q_prep(p, b, smem, warp - kSConvWarp0, lane);
         fence_proxy_async_smem();                    // the Q terms are read by the tensor core
         named_bar_sync(kSPrepBar, (kSThreads / 32 - kSConvWarp0) * 32);
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
         // ============================================================ operand tiles
-        if (warp < kSConvWarp0 + 4) {   // Q-term scales into this sub-partition: column 8 ps + 4 kk + q = word kk of row 32 q + lane
+        {   // Q-term scales into this sub-partition: column 8 ps + 4 kk + q = word kk of row 32 q + lane
             uint32_t v[16];
 #pragma unroll
             for (int ps = 0; ps < 2; ++ps)
@@ -398,10 +399,9 @@ __global__ void __launch_bounds__(kSThreads, 1) index_score_kernel(const ScorePa
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(SB_QREADY));
         }
-        const int m = (tid - kSConvWarp0 * 32) & (kITile - 1);   // key row of the tile this thread rewrites
-        const int cset = (warp - kSConvWarp0) >> 2;               // tiles j = cset mod kSConvSets
+        const int m = tid - kSConvWarp0 * 32;        // key row of the tile this thread rewrites
 #pragma unroll 1
-        for (int j = cset; j < n; j += kSConvSets) {
+        for (int j = 0; j < n; ++j) {
             const int s = j % kSStages, a = j % kSDepth, u = j / kSDepth;
             if (!mbar_wait(bar(SB_FULL + s), (j / kSStages) & 1, abort_flag, err)) break;
             if (u > 0 && !mbar_wait(bar(SB_AFREE + a), (u - 1) & 1, abort_flag, err)) break;
